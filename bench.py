@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark: Sinkhorn iterations per second of SinkSLOT's sparse solve on B200.
+
+Workload (one step = one Sinkhorn iteration = CSR row half-step + CSC column
+half-step): N = M = 2^20 points in d = 3, x ~ N(0, I), y ~ N(0, I) + 1.5 drawn
+from torch's CPU generator seeded with 1, uniform weights, eps = 0.01,
+L = 64 slices (seed 0), alternating variant.  Synthetic data of the headline
+configuration; the reference publishes no number for it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One process per GPU; for N > 1 launch under torch.distributed.run.  N > 1 runs
+one independent problem per rank (batch sharding: no data-path collective,
+weak scaling); the value is all ranks' iterations over the slowest rank's time.
+``--impl reference`` times the reference algorithm's CPU implementation (the
+C port in oracle/, all host threads) on the same workload; rank 0 only.
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "Sinkhorn iter/s at N=M=2^20,d=3,L=64 fp32; achieved HBM GB/s as % of peak"
+UNIT = "iter/s"
+WORKLOAD = dict(n=1 << 20, m=1 << 20, d=3, L=64, eps=0.01, n_iters=500, data_seed=1, shift=1.5,
+                proj_seed=0, variant="alternating")
+WORKLOAD_NAME = ("sinkslot sparse Sinkhorn, N=M=2^20, d=3, L=64, eps=0.01, alternating, "
+                 "x~N(0,I), y~N(0,I)+1.5 (seed 1), uniform weights")
+
+
+def measured_peak_gbs():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    p = os.path.join(ROOT, "profiles", "half_step_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+def make_inputs(rank: int):
+    w = WORKLOAD
+    torch.manual_seed(w["data_seed"] + 1000 * rank)
+    x = torch.randn(w["n"], w["d"])
+    y = torch.randn(w["m"], w["d"]) + w["shift"]
+    a = torch.full((w["n"],), 1.0 / w["n"])
+    b = torch.full((w["m"],), 1.0 / w["m"])
+    return x, y, a, b
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.lines = []
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            uuid = str(device_index)
+        self.cmd = ["nvidia-smi", f"--id={uuid}",
+                    "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                    "--format=csv,noheader,nounits", "-lms", "50"]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.15)
+
+    def stop(self):
+        if self.proc is None:
+            return self._summary([])
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        return self._summary(out.strip().splitlines())
+
+    @staticmethod
+    def _summary(lines):
+        sm, mx, reasons = [], [], set()
+        for ln in lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 3:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+                bits = int(parts[2], 16)
+            except ValueError:
+                continue
+            for bit, name in _REASONS.items():
+                if bits & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif gpus > 1:
+        raise SystemExit("--gpus > 1 needs torch.distributed.run (one process per GPU)")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------
+# the B200 arm
+# --------------------------------------------------------------------------
+def run_b200(args):
+    import sinkslot_b200
+    from sinkslot_b200 import sinkslot_solve
+    from sinkslot_b200.sinkhorn_solvers import seg_lse_online, sinkslot_alternating_b200
+    from sinkslot_b200.solver import cost_and_lam, sot_plan_coo, to_csr
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sinkslot_b200.load_library()
+    w = WORKLOAD
+    x, y, a, b = make_inputs(rank)
+    X, Y, A, B = (t.to(dev) for t in (x, y, a, b))
+
+    # setup (untimed for the iteration metric; reported)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    rows, cols, S = sot_plan_coo(X, Y, A, B, L=w["L"], seed=w["proj_seed"])
+    lam, _ = cost_and_lam(X, Y, rows, cols, S, w["eps"])
+    r_ptr, r_idx, r_lam, _ = to_csr(rows, cols, lam, w["n"])
+    c_ptr, c_idx, c_lam, _ = to_csr(cols, rows, lam, w["m"])
+    log_a, log_b = A.log(), B.log()
+    torch.cuda.synchronize(dev)
+    setup_ms = (time.perf_counter() - t0) * 1e3
+    nnz = int(rows.numel())
+    csr = (r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, w["n"], w["m"])
+
+    # warm-up, then exactly K timed iterations in one fused-loop call
+    sinkslot_alternating_b200(*csr, max(args.warmup, 0))
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    phi, psi, *_ = sinkslot_alternating_b200(*csr, args.steps)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world, dev)
+    value = world * args.steps / (ms / 1e3) if ms > 0 else 0.0
+
+    # dominant kernel: each half-step launch timed alone with events on its stream
+    reps = 20
+    dur = {"row": [], "col": []}
+    out_phi = torch.empty_like(log_a)
+    out_psi = torch.empty_like(log_b)
+    z_n, z_m = torch.zeros_like(log_a), torch.zeros_like(log_b)
+    for _ in range(reps):
+        for side in ("row", "col"):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if side == "row":
+                seg_lse_online(r_ptr, r_idx, r_lam, z_n, psi, w["n"], base=log_a, out=out_phi)
+            else:
+                seg_lse_online(c_ptr, c_idx, c_lam, z_m, phi, w["m"], base=log_b, out=out_psi)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            dur[side].append(e0.elapsed_time(e1))
+    s_idx = r_idx.element_size()
+    bytes_row = nnz * (s_idx + 4) + 16 * w["n"]
+    bytes_col = nnz * (c_idx.element_size() + 4) + 16 * w["m"]
+    t_row = statistics.median(dur["row"]) / 1e3
+    t_col = statistics.median(dur["col"]) / 1e3
+    achieved = (bytes_row + bytes_col) / (t_row + t_col) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    b_iter = bytes_row + bytes_col
+    traffic = ncu_traffic()
+
+    # end to end through the public API from pinned host buffers
+    xh, yh, ah, bh = (t.pin_memory() for t in (x, y, a, b))
+    phi_h = torch.empty(w["n"]).pin_memory()
+    psi_h = torch.empty(w["m"]).pin_memory()
+
+    def e2e_step():
+        Xd = xh.to(dev, non_blocking=True)
+        Yd = yh.to(dev, non_blocking=True)
+        Ad = ah.to(dev, non_blocking=True)
+        Bd = bh.to(dev, non_blocking=True)
+        r = sinkslot_solve(Xd, Yd, Ad, Bd, w["eps"], w["L"], w["proj_seed"], w["n_iters"])
+        phi_h.copy_(r.phi, non_blocking=True)
+        psi_h.copy_(r.psi, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e2e_steps = 3
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    q0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    q1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(q0.elapsed_time(q1), world, dev)
+    e2e_value = world * e2e_steps * w["n_iters"] / (e2e_ms / 1e3)
+    h2d = sum(t.numel() * t.element_size() for t in (x, y, a, b))
+    d2h = (w["n"] + w["m"]) * 4
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_from_support(rows, cols, lam, log_a, log_b, w)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD_NAME, "n": w["n"], "m": w["m"], "d": w["d"],
+                       "L": w["L"], "eps": w["eps"], "nnz": nnz,
+                       "parallelism": f"independent problem per GPU x{world}" if world > 1
+                       else "single GPU",
+                       "l2": "inputs larger than L2: %.2f GB of CSR+CSC streamed per iteration"
+                             % (2 * nnz * (s_idx + 4) / 1e9),
+                       "setup_ms": round(setup_ms, 1),
+                       "algorithmic_bytes_per_iter": b_iter,
+                       "iteration_gbs": round(b_iter * value / world / 1e9, 1)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": peak_kind,
+                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                         "kernel": "half_step_kernel (CSR row + CSC column launch, median of %d)"
+                                   % reps,
+                         "bytes_per_launch": {"row": bytes_row, "col": bytes_col},
+                         "launch_us": {"row": round(t_row * 1e6, 2),
+                                       "col": round(t_col * 1e6, 2)}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "step": "sinkslot_solve(...) from pinned host x, y, a, b: support build + "
+                            "%d iterations + potentials back" % w["n_iters"]},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def cpu_baseline_from_support(rows, cols, lam, log_a, log_b, w, budget_s: float = 15.0):
+    """The oracle's torch-backend iteration (C, OpenMP, all host threads) on the
+    same support, a bounded number of iterations."""
+    from oracle import oracle as O
+    O.build()
+    it = O.IterationTimer(rows.cpu().numpy(), cols.cpu().numpy(), lam.cpu().numpy(),
+                          log_a.cpu().numpy(), log_b.cpu().numpy(), w["n"], w["m"])
+    t0 = time.perf_counter()
+    it.run(1)
+    t1 = time.perf_counter() - t0
+    k = int(max(1, min(50, budget_s / max(t1, 1e-6))))
+    t0 = time.perf_counter()
+    it.run(k)
+    dt = time.perf_counter() - t0
+    it.close()
+    return {"value": round(k / dt, 4), "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+            "sample": f"{k} alternating iterations of the full workload (nnz={rows.numel()}) "
+                      f"after 1 untimed; support built once, untimed"}
+
+
+# --------------------------------------------------------------------------
+# the reference arm: the reference algorithm's CPU implementation (oracle port)
+# --------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    O.build()
+    w = WORKLOAD
+    x, y, a, b = make_inputs(0)
+    t0 = time.perf_counter()
+    rows, cols, S = O.sot_plan_coo(x.numpy(), y.numpy(), a.numpy(), b.numpy(), w["L"],
+                                   w["proj_seed"], builder="cuda_on_cpu")
+    cost = O.sqeuclid_cost(x.numpy(), y.numpy(), rows, cols)
+    lam = O.lam_values(S, cost, w["eps"])
+    setup_s = time.perf_counter() - t0
+    la = np.log(a.numpy()).astype(np.float32)
+    lb = np.log(b.numpy()).astype(np.float32)
+    it = O.IterationTimer(rows, cols, lam, la, lb, w["n"], w["m"])
+    it.run(1)  # warm-up (bounded: one iteration)
+    t0 = time.perf_counter()
+    it.run(1)
+    t1 = time.perf_counter() - t0
+    k = int(max(1, min(args.steps, 120.0 / max(t1, 1e-6))))
+    t0 = time.perf_counter()
+    it.run(k)
+    dt = time.perf_counter() - t0
+    it.close()
+    value = k / dt
+    cores = O.num_threads()
+    sample = (f"{k} of the requested {args.steps} alternating iterations of the full workload "
+              f"(nnz={rows.size}), after 2 untimed; support built once on the CPU "
+              f"({setup_s:.1f} s, untimed)")
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": k, "warmup": args.warmup, "ms_per_step": round(dt / k * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD_NAME, "n": w["n"], "m": w["m"], "d": w["d"],
+                   "L": w["L"], "eps": w["eps"], "nnz": int(rows.size),
+                   "parallelism": f"host CPU, {cores} threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--log2n", type=int, default=20,
+                    help="points per cloud = 2^log2n (20: the headline problem; smaller sizes "
+                         "are for profiling captures)")
+    args = ap.parse_args()
+    if args.log2n != 20:
+        global WORKLOAD_NAME
+        WORKLOAD["n"] = WORKLOAD["m"] = 1 << args.log2n
+        WORKLOAD_NAME = WORKLOAD_NAME.replace("N=M=2^20", f"N=M=2^{args.log2n}")
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,170 @@
+/*
+ * sinkslot_b200.h -- C ABI of the sm_100a SinkSLOT sparse-Sinkhorn backend
+ * (libsinkslot_b200.so).
+ *
+ * Conventions
+ *   - Every pointer argument is DEVICE memory unless its name ends in `_host`.
+ *   - `stream` is a cudaStream_t passed as void*; all work is enqueued on it.
+ *     Calls that return a count to the host (nnz, iterations, ...) synchronise
+ *     that stream, exactly where the reference reads a value back with
+ *     .item()/int()/bool().
+ *   - No call allocates device memory.  Scratch comes from a caller-provided
+ *     workspace whose size the matching *_workspace_bytes call reports.
+ *   - Return value: 0 on success, otherwise a status code (1 invalid argument,
+ *     2 CUDA error, 3 workspace too small, 4 unsupported); the message is in
+ *     sinkslot_last_error() (per calling thread).
+ *   - Reference paths are relative to cai4cai/SinkSLOT's torch-ext/ tree.
+ */
+#ifndef SINKSLOT_B200_H_
+#define SINKSLOT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Last error message of the calling thread ("" if none). */
+const char* sinkslot_last_error(void);
+
+/* ABI version (major * 100 + minor). */
+int sinkslot_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Support construction
+ * ------------------------------------------------------------------------- */
+
+/* Projections out[c, i] = <X[i, :], theta[c, :]> as the sequential fp32 FMA
+ * chain over d, slice-major (L, n).  Replaces `X @ th.T` in
+ * sinkslot/solver.py:221 (transposed to the (C, len) layout of
+ * `_ot_1d_coo_batched_cuda`, solver.py:117). */
+int sinkslot_project(const float* X, int64_t n, int d, const float* theta, int L, float* out,
+                     void* stream);
+
+int sinkslot_ot1d_workspace_bytes(int64_t n, int64_t m, int C, int64_t* bytes_host);
+
+/* One call of the batched 1-D north-west-corner builder over C slices:
+ * replaces `_ot_1d_coo_batched_cuda(PX, PY, a, b)`, sinkslot/solver.py:107-150.
+ * PXt (C, n) and PYt (C, m) are slice-major projections.  Writes the kept
+ * (R, Cc, mass) triples in the reference's emission order (slice-major, merged
+ * position ascending); capacity C * (n + m).  Optional (nullable) outputs: the
+ * per-slice argsort permutations ix (C, n) / iy (C, m) as uint32 and the
+ * cumsums ca (C, n) / cb (C, m).  *count_host receives the number of triples. */
+int sinkslot_ot1d_batched(const float* PXt, const float* PYt, const float* a, const float* b,
+                          int64_t n, int64_t m, int C, void* workspace, int64_t workspace_bytes,
+                          int64_t* R, int64_t* Cc, float* mass, uint32_t* ix, uint32_t* iy,
+                          float* ca, float* cb, int64_t* count_host, void* stream);
+
+int sinkslot_support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chunk,
+                                     int64_t* bytes_host);
+
+/* Sliced-lifted support: replaces `sot_plan_coo(X, Y, a, b, L, seed, chunk,
+ * ot1d=_ot_1d_coo_batched_cuda)`, sinkslot/solver.py:153-232.  theta (L, d)
+ * fp32 on the device holds get_random_projections(d, L, seed) cast to fp32
+ * (solver.py:193).  chunk <= 0 means all L slices in one batch.  The coalesced
+ * support stays in the workspace; *nnz_host receives its size.  Call
+ * sinkslot_support_export with the same sizes to read it out. */
+int sinkslot_build_support(const float* X, const float* Y, const float* a, const float* b,
+                           int64_t n, int64_t m, int d, const float* theta, int L, int chunk,
+                           void* workspace, int64_t workspace_bytes, int64_t* nnz_host,
+                           void* stream);
+
+/* rows, cols (int64) and S (fp32) of the support built by
+ * sinkslot_build_support, sorted by rows * m + cols: the return value of
+ * sot_plan_coo (solver.py:232). */
+int sinkslot_support_export(const void* workspace, int64_t workspace_bytes, int64_t n, int64_t m,
+                            int d, int L, int chunk, int64_t nnz, int64_t* rows, int64_t* cols,
+                            float* S, void* stream);
+
+int sinkslot_csr_workspace_bytes(int64_t nnz, int64_t nseg, int64_t* bytes_host);
+
+/* COO -> CSR: replaces `to_csr(rows, cols, vals, n, narrow_key)`,
+ * sinkslot/solver.py:235-276.  Stable by `seg`; identity permutation when
+ * `seg` is already non-decreasing (*was_sorted_host = 1).  Writes indptr
+ * (nseg + 1, int32), idx = other[perm] as int16 (idx_bytes 2) or int32
+ * (idx_bytes 4), vals[perm] (vals/out_vals nullable) and perm (int64,
+ * nullable). */
+int sinkslot_coo_to_csr(const int64_t* seg, const int64_t* other, const float* vals, int64_t nnz,
+                        int64_t nseg, int idx_bytes, void* workspace, int64_t workspace_bytes,
+                        int32_t* indptr, void* idx, float* out_vals, int64_t* perm,
+                        int* was_sorted_host, void* stream);
+
+/* max(v) over n int64 (0 if n == 0): the `int(idx.max())` of solver.py:275.
+ * workspace: 8 bytes. */
+int sinkslot_max_index(const int64_t* v, int64_t n, void* workspace, int64_t* max_host,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Cost and the Sinkhorn iteration
+ * ------------------------------------------------------------------------- */
+
+/* cost[k] = ||x[rows[k]] - y[cols[k]]||^2 and lam[k] = log(max(S[k], tiny)) -
+ * cost[k] / eps.  Replaces `sparse_sqeuclidean_cost` (sinkslot/solver.py:303-360)
+ * and the `lam` line of sinkslot_solve (sinkslot/sinkhorn_solvers.py:700).
+ * lam / cost / S are nullable (lam needs S). */
+int sinkslot_cost_lam(const float* x, const float* y, int d, const int64_t* rows,
+                      const int64_t* cols, const float* S, int64_t nnz, double eps, float* lam,
+                      float* cost, void* stream);
+
+/* Segmented log-sum-exp half-step: out[s] = base[s] - LSE_{k in s}((lam[k] +
+ * selfpot[s]) + other[idx[k]]) (out[s] = LSE when base is NULL; selfpot is
+ * nullable and then zero).  Replaces `seg_lse_online(indptr, colidx, lam, phi,
+ * psi, n, ..., base, out)`, sinkslot/sinkhorn_solvers.py:121-146, whose `phi`
+ * is selfpot here (all-zero in the reference loops, :229). */
+int sinkslot_seg_lse(const int32_t* indptr, const void* idx, int idx_bytes, const float* lam,
+                     int64_t nnz, const float* selfpot, const float* other, const float* base,
+                     int64_t nseg, float* out, void* stream);
+
+/* Scratch floats sinkslot_solve_csr needs for an (n, m) problem. */
+int sinkslot_solve_work_floats(int64_t n, int64_t m, int64_t* floats_host);
+
+/* Full Sinkhorn loop over prebuilt CSR (rows) / CSC (cols): replaces
+ * `sinkslot_alternating_triton` (variant 0) and `sinkslot_symmetric_triton`
+ * (variant 1), sinkslot/sinkhorn_solvers.py:195-419, with the semantics of
+ * their torch twins (:443-588).  stop_mode: 0 fixed (n_iters), 1 potential,
+ * 2 marginal (up to max_iter, checked every check_every).  phi (n), psi (m)
+ * receive the absorbed potentials.  *converged_host: -1 (fixed mode), 0 or 1;
+ * *final_viol_host: NaN in fixed mode. */
+int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
+                       const float* r_lam, const int32_t* c_ptr, const void* c_idx,
+                       int c_idx_bytes, const float* c_lam, int64_t nnz, const float* log_a,
+                       const float* log_b, int64_t n, int64_t m, int variant, int stop_mode,
+                       int64_t n_iters, int64_t max_iter, int64_t check_every, double tol,
+                       double eps, double alpha, float* phi, float* psi, float* work,
+                       int64_t work_floats, int64_t* iters_host, int* converged_host,
+                       double* final_viol_host, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Plan export and gradient
+ * ------------------------------------------------------------------------- */
+
+/* Plan values exp(phi[r] + psi[c] + log S - cost / eps), cost recomputed from
+ * x, y.  grad_form 0: `((phi[r] + psi[c]) + log_S) - cost/eps` as in
+ * sparse_transport_plan (sinkslot/sinkhorn_solvers.py:757-758); grad_form 1:
+ * `(phi[r] + psi[c]) + (log_S - cost/eps)` as in slot_grad / _SLOTCostFn
+ * (sinkslot/gradient.py:94-97, sinkslot/samples_loss.py:69-73). */
+int sinkslot_plan_values(const float* phi, const float* psi, const int64_t* rows,
+                         const int64_t* cols, const float* S, const float* x, const float* y,
+                         int d, int64_t nnz, double eps, int grad_form, float* out, void* stream);
+
+int sinkslot_barycentric_workspace_bytes(int64_t n, int64_t m, int d, int64_t* bytes_host);
+
+/* Barycentric projections of a sparse plan and the envelope gradient:
+ * replaces `sparse_barycentric_map(T_vals, rows, cols, x, y)` (sinkslot/gradient.py:25-61)
+ * and `2 * a[:, None] * (X - Tx)` (gradient.py:99, samples_loss.py:82).
+ * Tx (n, d), Ty (m, d), grad (n, d) are nullable; grad needs a.  d <= 16. */
+int sinkslot_barycentric(const float* T, const int64_t* rows, const int64_t* cols, int64_t nnz,
+                         const float* x, const float* y, int64_t n, int64_t m, int d,
+                         const float* a, float* Tx, float* Ty, float* grad, void* workspace,
+                         int64_t workspace_bytes, void* stream);
+
+/* dual value <phi, a> + <psi, b> accumulated in fp64 into out[0] (device);
+ * the caller multiplies by eps (sinkslot/samples_loss.py:74). */
+int sinkslot_dual_value(const float* phi, const float* a, int64_t n, const float* psi,
+                        const float* b, int64_t m, double* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SINKSLOT_B200_H_ */

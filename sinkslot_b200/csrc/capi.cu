@@ -1,0 +1,229 @@
+// capi.cu -- extern "C" entry points of libsinkslot_b200.so (declared in
+// include/sinkslot_b200.h).  Thin argument checks + dispatch to the launchers.
+#include <string>
+
+#include "../../include/sinkslot_b200.h"
+#include "common.cuh"
+#include "export.h"
+#include "primitives.h"
+#include "sinkhorn.h"
+#include "support.h"
+
+namespace sinkslot {
+
+static thread_local std::string g_last_error;
+void set_error(const std::string& msg) { g_last_error = msg; }
+const char* last_error() { return g_last_error.c_str(); }
+
+}  // namespace sinkslot
+
+using namespace sinkslot;
+
+#define ST(s) static_cast<cudaStream_t>(s)
+
+// Clear the previous message, run, and keep the message only on failure.
+#define CAPI_BODY(expr)        \
+  do {                         \
+    g_last_error_clear();      \
+    return (expr);             \
+  } while (0)
+
+static void g_last_error_clear() { set_error(""); }
+
+extern "C" {
+
+const char* sinkslot_last_error(void) { return last_error(); }
+
+int sinkslot_abi_version(void) { return 100; }
+
+int sinkslot_project(const float* X, int64_t n, int d, const float* theta, int L, float* out,
+                     void* stream) {
+  CAPI_BODY(project(X, n, d, theta, L, out, ST(stream)));
+}
+
+int sinkslot_ot1d_workspace_bytes(int64_t n, int64_t m, int C, int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && n >= 1 && m >= 1 && C >= 1, "ot1d_workspace_bytes: bad args");
+  *bytes_host = (int64_t)ot1d_workspace_bytes(n, m, C);
+  return kOk;
+}
+
+int sinkslot_ot1d_batched(const float* PXt, const float* PYt, const float* a, const float* b,
+                          int64_t n, int64_t m, int C, void* workspace, int64_t workspace_bytes,
+                          int64_t* R, int64_t* Cc, float* mass, uint32_t* ix, uint32_t* iy,
+                          float* ca, float* cb, int64_t* count_host, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(PXt && PYt && a && b && R && Cc && mass && count_host && workspace,
+                   "ot1d_batched: null argument");
+  return ot1d_batched(PXt, PYt, a, b, n, m, C, workspace, (size_t)workspace_bytes, R, Cc, mass, ix,
+                      iy, ca, cb, count_host, ST(stream));
+}
+
+int sinkslot_support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chunk,
+                                     int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && n >= 1 && m >= 1 && d >= 1 && L >= 1,
+                   "support_workspace_bytes: bad args");
+  *bytes_host = (int64_t)support_workspace_bytes(n, m, d, L, chunk);
+  return kOk;
+}
+
+int sinkslot_build_support(const float* X, const float* Y, const float* a, const float* b,
+                           int64_t n, int64_t m, int d, const float* theta, int L, int chunk,
+                           void* workspace, int64_t workspace_bytes, int64_t* nnz_host,
+                           void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(X && Y && a && b && theta && workspace && nnz_host,
+                   "build_support: null argument");
+  return build_support(X, Y, a, b, n, m, d, theta, L, chunk, workspace, (size_t)workspace_bytes,
+                       nnz_host, ST(stream));
+}
+
+int sinkslot_support_export(const void* workspace, int64_t workspace_bytes, int64_t n, int64_t m,
+                            int d, int L, int chunk, int64_t nnz, int64_t* rows, int64_t* cols,
+                            float* S, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(workspace && (nnz == 0 || (rows && cols && S)), "support_export: null argument");
+  return support_export(workspace, (size_t)workspace_bytes, n, m, d, L, chunk, nnz, rows, cols, S,
+                        ST(stream));
+}
+
+int sinkslot_csr_workspace_bytes(int64_t nnz, int64_t nseg, int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && nnz >= 0 && nseg >= 0, "csr_workspace_bytes: bad args");
+  *bytes_host = (int64_t)csr_workspace_bytes(nnz, nseg);
+  return kOk;
+}
+
+int sinkslot_coo_to_csr(const int64_t* seg, const int64_t* other, const float* vals, int64_t nnz,
+                        int64_t nseg, int idx_bytes, void* workspace, int64_t workspace_bytes,
+                        int32_t* indptr, void* idx, float* out_vals, int64_t* perm,
+                        int* was_sorted_host, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(indptr && was_sorted_host && workspace && (nnz == 0 || (seg && other && idx)),
+                   "to_csr: null argument");
+  SINKSLOT_REQUIRE(vals == nullptr || out_vals != nullptr, "to_csr: vals given without out_vals");
+  return coo_to_csr(seg, other, vals, nnz, nseg, idx_bytes, workspace, (size_t)workspace_bytes,
+                    indptr, idx, vals ? out_vals : nullptr, perm, was_sorted_host, ST(stream));
+}
+
+int sinkslot_max_index(const int64_t* v, int64_t n, void* workspace, int64_t* max_host,
+                       void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(workspace && max_host && (n == 0 || v), "max_index: null argument");
+  return max_index(v, n, workspace, max_host, ST(stream));
+}
+
+int sinkslot_cost_lam(const float* x, const float* y, int d, const int64_t* rows,
+                      const int64_t* cols, const float* S, int64_t nnz, double eps, float* lam,
+                      float* cost, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(nnz == 0 || (x && y && rows && cols), "cost_lam: null argument");
+  SINKSLOT_REQUIRE(lam == nullptr || eps != 0.0, "cost_lam: eps must be nonzero");
+  return cost_lam(x, y, d, rows, cols, S, nnz, eps, lam, cost, ST(stream));
+}
+
+int sinkslot_seg_lse(const int32_t* indptr, const void* idx, int idx_bytes, const float* lam,
+                     int64_t nnz, const float* selfpot, const float* other, const float* base,
+                     int64_t nseg, float* out, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(indptr && out && (nnz == 0 || (idx && lam && other)), "seg_lse: null argument");
+  HalfStep h;
+  h.ptr = indptr;
+  h.idx = idx;
+  h.idx_bytes = idx_bytes;
+  h.lam = lam;
+  h.nseg = nseg;
+  h.nnz = nnz;
+  h.other = other;
+  h.selfpot = selfpot;
+  h.base = base;
+  h.out = out;
+  h.self_old = out;
+  return half_step(h, 0, 0, ST(stream));
+}
+
+int sinkslot_solve_work_floats(int64_t n, int64_t m, int64_t* floats_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(floats_host && n >= 0 && m >= 0, "solve_work_floats: bad args");
+  *floats_host = (int64_t)solve_work_floats(n, m);
+  return kOk;
+}
+
+int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
+                       const float* r_lam, const int32_t* c_ptr, const void* c_idx,
+                       int c_idx_bytes, const float* c_lam, int64_t nnz, const float* log_a,
+                       const float* log_b, int64_t n, int64_t m, int variant, int stop_mode,
+                       int64_t n_iters, int64_t max_iter, int64_t check_every, double tol,
+                       double eps, double alpha, float* phi, float* psi, float* work,
+                       int64_t work_floats, int64_t* iters_host, int* converged_host,
+                       double* final_viol_host, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(r_ptr && c_ptr && log_a && log_b && phi && psi && work && iters_host &&
+                       converged_host && final_viol_host,
+                   "solve_csr: null argument");
+  SINKSLOT_REQUIRE(nnz == 0 || (r_idx && r_lam && c_idx && c_lam), "solve_csr: null argument");
+  SolveSpec sp;
+  sp.row.ptr = r_ptr;
+  sp.row.idx = r_idx;
+  sp.row.idx_bytes = r_idx_bytes;
+  sp.row.lam = r_lam;
+  sp.row.nseg = n;
+  sp.row.nnz = nnz;
+  sp.col.ptr = c_ptr;
+  sp.col.idx = c_idx;
+  sp.col.idx_bytes = c_idx_bytes;
+  sp.col.lam = c_lam;
+  sp.col.nseg = m;
+  sp.col.nnz = nnz;
+  sp.log_a = log_a;
+  sp.log_b = log_b;
+  sp.variant = variant;
+  sp.mode = stop_mode;
+  sp.n_iters = n_iters;
+  sp.max_iter = max_iter;
+  sp.check_every = check_every;
+  sp.tol = tol;
+  sp.eps = eps;
+  sp.alpha = alpha;
+  return solve_loop(sp, phi, psi, work, work_floats, iters_host, converged_host, final_viol_host,
+                    ST(stream));
+}
+
+int sinkslot_plan_values(const float* phi, const float* psi, const int64_t* rows,
+                         const int64_t* cols, const float* S, const float* x, const float* y,
+                         int d, int64_t nnz, double eps, int grad_form, float* out, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(nnz == 0 || (phi && psi && rows && cols && S && x && y && out),
+                   "plan_values: null argument");
+  SINKSLOT_REQUIRE(eps != 0.0, "plan_values: eps must be nonzero");
+  return plan_values(phi, psi, rows, cols, S, x, y, d, nnz, eps, grad_form, out, ST(stream));
+}
+
+int sinkslot_barycentric_workspace_bytes(int64_t n, int64_t m, int d, int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && n >= 0 && m >= 0 && d >= 1, "barycentric_workspace_bytes: bad args");
+  *bytes_host = (int64_t)bary_workspace_bytes(n, m, d);
+  return kOk;
+}
+
+int sinkslot_barycentric(const float* T, const int64_t* rows, const int64_t* cols, int64_t nnz,
+                         const float* x, const float* y, int64_t n, int64_t m, int d,
+                         const float* a, float* Tx, float* Ty, float* grad, void* workspace,
+                         int64_t workspace_bytes, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(workspace && x && y && (nnz == 0 || (T && rows && cols)),
+                   "barycentric: null argument");
+  return barycentric(T, rows, cols, nnz, x, y, n, m, d, a, Tx, Ty, grad, workspace,
+                     (size_t)workspace_bytes, ST(stream));
+}
+
+int sinkslot_dual_value(const float* phi, const float* a, int64_t n, const float* psi,
+                        const float* b, int64_t m, double* out, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(out && (n == 0 || (phi && a)) && (m == 0 || (psi && b)),
+                   "dual_value: null argument");
+  return dual_value(phi, a, n, psi, b, m, out, ST(stream));
+}
+
+}  // extern "C"

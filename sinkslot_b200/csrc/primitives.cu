@@ -1,0 +1,253 @@
+// primitives.cu -- device-wide exclusive scan and a stable, segmented LSD radix
+// sort (8-bit digits).  Both are HBM-bound integer passes: tiles of 4096 keys,
+// 256-thread blocks, warp-level match/ballot ranking for stability.
+#include "common.cuh"
+#include "primitives.h"
+
+namespace sinkslot {
+
+// --------------------------------------------------------------------------
+// Exclusive scan (int64): 8192 elements per block, recursive over block sums.
+// --------------------------------------------------------------------------
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ int64_t warp_incl_scan(int64_t v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int64_t t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_block_kernel(int64_t* data, int64_t n,
+                                                                  int64_t* block_sums) {
+  __shared__ int64_t warp_tot[kScanThreads / 32];
+  const int64_t base = (int64_t)blockIdx.x * kScanTile + (int64_t)threadIdx.x * kScanItems;
+  int64_t v[kScanItems];
+  int64_t run = 0;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    const int64_t p = base + i;
+    v[i] = p < n ? data[p] : 0;
+    const int64_t t = v[i];
+    v[i] = run;  // exclusive within the thread
+    run += t;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int64_t incl = warp_incl_scan(run, lane);
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t w = lane < kScanThreads / 32 ? warp_tot[lane] : 0;
+    int64_t wi = warp_incl_scan(w, lane);
+    if (lane < kScanThreads / 32) warp_tot[lane] = wi - w;
+    if (lane == 31 && block_sums) block_sums[blockIdx.x] = wi;
+  }
+  __syncthreads();
+  const int64_t off = warp_tot[warp] + incl - run;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    const int64_t p = base + i;
+    if (p < n) data[p] = v[i] + off;
+  }
+}
+
+__global__ void scan_add_kernel(int64_t* data, int64_t n, const int64_t* block_offsets) {
+  const int64_t add = block_offsets[blockIdx.x];
+  const int64_t base = (int64_t)blockIdx.x * kScanTile;
+  for (int i = threadIdx.x; i < kScanTile; i += blockDim.x) {
+    const int64_t p = base + i;
+    if (p < n) data[p] += add;
+  }
+}
+
+__global__ void scan_total_kernel(const int64_t* data_excl, const int64_t* last_in, int64_t n,
+                                  int64_t* total) {
+  total[0] = data_excl[n - 1] + last_in[0];
+}
+
+size_t scan_tmp_elems(int64_t n) {
+  size_t t = 1;  // saved last element
+  int64_t m = n;
+  while (m > kScanTile) {
+    m = ceil_div64(m, kScanTile);
+    t += (size_t)m + 1;
+  }
+  return t + 1;
+}
+
+static int scan_rec(int64_t* data, int64_t n, int64_t* tmp, cudaStream_t stream) {
+  const int64_t nb = ceil_div64(n, kScanTile);
+  if (nb <= 1) {
+    scan_block_kernel<<<1, kScanThreads, 0, stream>>>(data, n, nullptr);
+    SINKSLOT_CHECK_LAUNCH();
+    return kOk;
+  }
+  int64_t* sums = tmp;
+  scan_block_kernel<<<(unsigned)nb, kScanThreads, 0, stream>>>(data, n, sums);
+  SINKSLOT_CHECK_LAUNCH();
+  SINKSLOT_TRY(scan_rec(sums, nb, tmp + nb + 1, stream));
+  scan_add_kernel<<<(unsigned)nb, 256, 0, stream>>>(data, n, sums);
+  SINKSLOT_CHECK_LAUNCH();
+  return kOk;
+}
+
+int scan_exclusive_i64(int64_t* data, int64_t n, int64_t* tmp, int64_t* total,
+                       cudaStream_t stream) {
+  if (n <= 0) {
+    if (total) SINKSLOT_CUDA_TRY(cudaMemsetAsync(total, 0, sizeof(int64_t), stream));
+    return kOk;
+  }
+  int64_t* last = tmp;  // keep the last input for the total
+  if (total)
+    SINKSLOT_CUDA_TRY(cudaMemcpyAsync(last, data + n - 1, sizeof(int64_t),
+                                      cudaMemcpyDeviceToDevice, stream));
+  SINKSLOT_TRY(scan_rec(data, n, tmp + 1, stream));
+  if (total) {
+    scan_total_kernel<<<1, 1, 0, stream>>>(data, last, n, total);
+    SINKSLOT_CHECK_LAUNCH();
+  }
+  return kOk;
+}
+
+// --------------------------------------------------------------------------
+// Radix sort
+// --------------------------------------------------------------------------
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortItems = 16;
+constexpr int kSortTile = kSortThreads * kSortItems;  // 4096 keys per tile
+constexpr int kRadix = 256;
+
+int64_t radix_hist_elems(int64_t nseg, int64_t seglen) {
+  return nseg * kRadix * ceil_div64(seglen, kSortTile);
+}
+
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const K* __restrict__ keys,
+                                                                  int64_t seglen, int ntiles,
+                                                                  int shift,
+                                                                  int64_t* __restrict__ hist) {
+  __shared__ uint32_t wh[kSortWarps][kRadix];
+  const int seg = blockIdx.y, tile = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&wh[0][0])[i] = 0;
+  __syncthreads();
+  const K* segk = keys + (int64_t)seg * seglen;
+  const int64_t chunk = (int64_t)tile * kSortTile + (int64_t)warp * 32 * kSortItems;
+#pragma unroll 4
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = chunk + r * 32 + lane;
+    if (idx < seglen) {
+      const uint32_t dg = (uint32_t)(segk[idx] >> shift) & 0xFFu;
+      atomicAdd(&wh[warp][dg], 1u);
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < kRadix; d += kSortThreads) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) t += wh[w][d];
+    hist[((int64_t)seg * kRadix + d) * ntiles + tile] = t;
+  }
+}
+
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
+    const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, K* __restrict__ keys_out,
+    uint32_t* __restrict__ vals_out, int64_t seglen, int ntiles, int shift,
+    const int64_t* __restrict__ offs) {
+  __shared__ uint32_t wcnt[kSortWarps][kRadix];
+  __shared__ int64_t wbase[kSortWarps][kRadix];
+  const int seg = blockIdx.y, tile = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t segbase = (int64_t)seg * seglen;
+  const int64_t chunk = (int64_t)tile * kSortTile + (int64_t)warp * 32 * kSortItems;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  K key[kSortItems];
+  uint32_t val[kSortItems];
+  uint32_t loc[kSortItems];
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = chunk + r * 32 + lane;
+    const bool valid = idx < seglen;
+    key[r] = valid ? keys_in[segbase + idx] : K(0);
+    val[r] = valid ? (vals_in ? vals_in[segbase + idx] : (uint32_t)idx) : 0u;
+    const uint32_t dg = valid ? ((uint32_t)(key[r] >> shift) & 0xFFu) : 0x100u;
+    const uint32_t peers = __match_any_sync(0xffffffffu, dg);
+    const uint32_t rank = __popc(peers & lt_mask);
+    uint32_t base = 0;
+    if (valid) base = wcnt[warp][dg];
+    __syncwarp();
+    if (valid && rank == 0) wcnt[warp][dg] = base + __popc(peers);
+    __syncwarp();
+    loc[r] = base + rank;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < kRadix; d += kSortThreads) {
+    int64_t run = offs[((int64_t)seg * kRadix + d) * ntiles + tile];
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      wbase[w][d] = run;
+      run += wcnt[w][d];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = chunk + r * 32 + lane;
+    if (idx < seglen) {
+      const uint32_t dg = (uint32_t)(key[r] >> shift) & 0xFFu;
+      const int64_t pos = wbase[warp][dg] + loc[r];
+      keys_out[pos] = key[r];
+      vals_out[pos] = val[r];
+    }
+  }
+}
+
+template <typename K>
+int radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, bool identity_vals,
+                     int64_t nseg, int64_t seglen, int key_bits, int64_t* hist, int64_t* scan_tmp,
+                     bool* result_in_alt, cudaStream_t stream) {
+  *result_in_alt = false;
+  SINKSLOT_REQUIRE(keys && vals && keys_alt && vals_alt, "radix sort: null buffer");
+  if (nseg <= 0 || seglen <= 0) return kOk;
+  SINKSLOT_REQUIRE(nseg <= 65535, "radix sort: too many segments");
+  const int64_t ntiles = ceil_div64(seglen, kSortTile);
+  SINKSLOT_REQUIRE(ntiles <= 0x7fffffff, "radix sort: segment too long");
+  const int64_t nh = nseg * kRadix * ntiles;
+  if (key_bits < 1) key_bits = 1;
+  K* kin = keys;
+  uint32_t* vin = vals;
+  K* kout = keys_alt;
+  uint32_t* vout = vals_alt;
+  bool first = true;
+  bool in_alt = false;
+  for (int shift = 0; shift < key_bits; shift += 8) {
+    dim3 grid((unsigned)ntiles, (unsigned)nseg);
+    radix_hist_kernel<K><<<grid, kSortThreads, 0, stream>>>(kin, seglen, (int)ntiles, shift, hist);
+    SINKSLOT_CHECK_LAUNCH();
+    SINKSLOT_TRY(scan_exclusive_i64(hist, nh, scan_tmp, nullptr, stream));
+    radix_scatter_kernel<K><<<grid, kSortThreads, 0, stream>>>(
+        kin, (first && identity_vals) ? nullptr : vin, kout, vout, seglen, (int)ntiles, shift, hist);
+    SINKSLOT_CHECK_LAUNCH();
+    first = false;
+    K* tk = kin; kin = kout; kout = tk;
+    uint32_t* tv = vin; vin = vout; vout = tv;
+    in_alt = !in_alt;
+  }
+  *result_in_alt = in_alt;
+  return kOk;
+}
+
+template int radix_sort_pairs<uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*, bool, int64_t,
+                                        int64_t, int, int64_t*, int64_t*, bool*, cudaStream_t);
+template int radix_sort_pairs<uint64_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*, bool, int64_t,
+                                        int64_t, int, int64_t*, int64_t*, bool*, cudaStream_t);
+
+}  // namespace sinkslot

@@ -1,0 +1,329 @@
+// sinkhorn.cu -- fused segmented log-sum-exp half-steps and the solve loops.
+//
+// One half-step (reference: `_seg_lse_online_kernel`, sinkhorn_solvers.py:45-94,
+// and `_seg_lse_coo`, :427-440) computes for every segment s of a CSR/CSC:
+//
+//     res[s] = base[s] - log sum_{k in s} exp(lam[k] + other[idx[k]])
+//
+// A group of G lanes (G = 4..32, from the mean segment length) owns one segment,
+// streams idx/lam once with evict-first loads (they are read once per half-step;
+// the gathered potential stays L2-resident), keeps a running (max, sum) per lane
+// and merges the G partial pairs with shuffles.  Fused into the same pass:
+//   * the write mode: plain store, the symmetric variant's alpha-blend into a
+//     second buffer (sinkhorn_solvers.py:361-363), or no store (check only);
+//   * the stop-criterion reduction (sinkhorn_solvers.py:246-288, 373-418): the
+//     marginal proxy |a*exp(old-new) - a| or the potential change |new - prev|,
+//     max-reduced into one device word per side.
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+#include "sinkhorn.h"
+
+namespace sinkslot {
+
+enum OutMode { kOutPlain = 0, kOutBlend = 1, kOutNone = 2 };
+enum CheckMode { kChkNone = 0, kChkMarg = 1, kChkPot = 2 };
+
+constexpr int kLseThreads = 256;
+constexpr int kLseUnroll = 4;
+
+template <typename IT, int G, int OUT, int CHK>
+__global__ void __launch_bounds__(kLseThreads) half_step_kernel(
+    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, const float* __restrict__ lam,
+    const float* __restrict__ other, const float* __restrict__ selfpot,
+    const float* __restrict__ base,
+    const float* self_old, float* out, int64_t nseg, float w_old, float w_new, float* prev,
+    uint32_t* acc) {
+  // self_old and out alias in the Gauss-Seidel variant (in-place update): no
+  // __restrict__ on either, so the old value is read before the store.
+  const int lane = threadIdx.x & (G - 1);
+  const int64_t groups = ((int64_t)gridDim.x * kLseThreads) / G;
+  uint32_t chk_bits = 0;
+  // The segment loop is warp-uniform (it steps the warp's first segment) so the
+  // full-mask shuffles below always see all 32 lanes; idle groups at the tail
+  // run with an empty range and store nothing.
+  const int64_t warp_first = ((int64_t)blockIdx.x * kLseThreads + (threadIdx.x & ~31)) / G;
+  const int group_in_warp = (threadIdx.x & 31) / G;
+  for (int64_t wseg = warp_first; wseg < nseg; wseg += groups) {
+    const int64_t seg = wseg + group_in_warp;
+    const bool active = seg < nseg;
+    const int64_t start = active ? ptr[seg] : 0, end = active ? ptr[seg + 1] : 0;
+    // term = (lam + p) + other[idx]: the reference kernel's `v + p + q`, with
+    // p = 0 in every solve loop (lam + 0 is exact, so the loops see lam + q)
+    const float p = (selfpot && active) ? selfpot[seg] : 0.0f;
+    float mx = -INFINITY, sm = 0.0f;
+    for (int64_t k0 = start; k0 < end; k0 += G * kLseUnroll) {
+      float v[kLseUnroll];
+      int64_t kk[kLseUnroll];
+      IT ci[kLseUnroll];
+      float lv[kLseUnroll];
+#pragma unroll
+      for (int u = 0; u < kLseUnroll; ++u) {
+        kk[u] = k0 + u * G + lane;
+        ci[u] = kk[u] < end ? ld_stream(idx + kk[u]) : IT(0);
+        lv[u] = kk[u] < end ? ld_stream(lam + kk[u]) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kLseUnroll; ++u)
+        v[u] = kk[u] < end ? __fadd_rn(__fadd_rn(lv[u], p), __ldg(other + (int64_t)ci[u])) : -INFINITY;
+      float bm = v[0];
+#pragma unroll
+      for (int u = 1; u < kLseUnroll; ++u) bm = fmaxf(bm, v[u]);
+      const float nm = fmaxf(mx, bm);
+      if (nm == -INFINITY) continue;
+      float s2 = 0.0f;
+#pragma unroll
+      for (int u = 0; u < kLseUnroll; ++u) s2 += __expf(v[u] - nm);
+      sm = sm * __expf(mx - nm) + s2;
+      mx = nm;
+    }
+#pragma unroll
+    for (int o = G / 2; o >= 1; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, mx, o, G);
+      const float os = __shfl_xor_sync(0xffffffffu, sm, o, G);
+      const float nm = fmaxf(mx, om);
+      if (nm == -INFINITY) {
+        sm = 0.0f;
+      } else {
+        sm = sm * __expf(mx - nm) + os * __expf(om - nm);
+      }
+      mx = nm;
+    }
+    if (lane == 0 && active) {
+      const float lse = sm > 0.0f ? mx + logf(fmaxf(sm, FLT_MIN)) : -INFINITY;
+      const float b = base ? base[seg] : 0.0f;
+      const float res = base ? __fsub_rn(b, lse) : lse;
+      float nv = res;
+      float old = 0.0f;
+      if (OUT == kOutBlend || CHK == kChkMarg) old = self_old[seg];
+      if (OUT == kOutBlend) nv = __fadd_rn(__fmul_rn(w_old, old), __fmul_rn(w_new, res));
+      if (OUT != kOutNone) out[seg] = nv;
+      if (CHK == kChkMarg) {
+        const float ea = expf(b);
+        const float t = __fmul_rn(ea, expf(__fsub_rn(old, res)));
+        chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(t, ea)));
+      } else if (CHK == kChkPot) {
+        chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(nv, prev[seg])));
+        prev[seg] = nv;
+      }
+    }
+  }
+  if (CHK != kChkNone) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) chk_bits = max(chk_bits, __shfl_xor_sync(0xffffffffu, chk_bits, o));
+    if ((threadIdx.x & 31) == 0 && chk_bits) atomicMax(acc, chk_bits);
+  }
+}
+
+static int pick_group(int64_t nnz, int64_t nseg) {
+  const int64_t mean = nseg > 0 ? (nnz + nseg - 1) / nseg : 1;
+  int g = 4;
+  while (g < 32 && (int64_t)g * kLseUnroll < mean) g <<= 1;
+  return g;
+}
+
+template <typename IT, int G>
+static void launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
+  const int64_t want = ceil_div64(h.nseg * G, kLseThreads);
+  const int64_t cap = (int64_t)num_sms() * 16;
+  const unsigned grid = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
+  const IT* idx = static_cast<const IT*>(h.idx);
+#define SINKSLOT_HS(OUTM, CHKM)                                                           \
+  half_step_kernel<IT, G, OUTM, CHKM><<<grid, kLseThreads, 0, st>>>(                      \
+      h.ptr, idx, h.lam, h.other, h.selfpot, h.base, h.self_old, h.out, h.nseg, h.w_old, h.w_new, \
+      h.prev, h.acc)
+  if (out_mode == kOutPlain) {
+    if (chk == kChkNone) SINKSLOT_HS(kOutPlain, kChkNone);
+    else if (chk == kChkMarg) SINKSLOT_HS(kOutPlain, kChkMarg);
+    else SINKSLOT_HS(kOutPlain, kChkPot);
+  } else if (out_mode == kOutBlend) {
+    if (chk == kChkNone) SINKSLOT_HS(kOutBlend, kChkNone);
+    else if (chk == kChkMarg) SINKSLOT_HS(kOutBlend, kChkMarg);
+    else SINKSLOT_HS(kOutBlend, kChkPot);
+  } else {
+    SINKSLOT_HS(kOutNone, kChkMarg);
+  }
+#undef SINKSLOT_HS
+}
+
+template <typename IT>
+static void launch_it(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
+  switch (h.group) {
+    case 4: launch_g<IT, 4>(h, out_mode, chk, st); break;
+    case 8: launch_g<IT, 8>(h, out_mode, chk, st); break;
+    case 16: launch_g<IT, 16>(h, out_mode, chk, st); break;
+    default: launch_g<IT, 32>(h, out_mode, chk, st); break;
+  }
+}
+
+int half_step(const HalfStep& h0, int out_mode, int chk, cudaStream_t st) {
+  SINKSLOT_REQUIRE(h0.idx_bytes == 2 || h0.idx_bytes == 4, "half step: idx_bytes must be 2 or 4");
+  SINKSLOT_REQUIRE(out_mode != kOutNone || chk == kChkMarg, "half step: check-only needs a check");
+  if (h0.nseg <= 0) return kOk;
+  HalfStep h = h0;
+  if (h.group == 0) h.group = pick_group(h.nnz, h.nseg);
+  if (h.idx_bytes == 2) launch_it<int16_t>(h, out_mode, chk, st);
+  else launch_it<int32_t>(h, out_mode, chk, st);
+  SINKSLOT_CHECK_LAUNCH();
+  return kOk;
+}
+
+// --------------------------------------------------------------------------
+// Solve loops (host logic mirrors sinkhorn_solvers.py:195-419 exactly:
+// iteration counting, check cadence, tol comparisons in double).
+// --------------------------------------------------------------------------
+static int read_acc(const uint32_t* d_acc, double* a0, double* a1, cudaStream_t st) {
+  uint32_t h[2];
+  SINKSLOT_CUDA_TRY(cudaMemcpyAsync(h, d_acc, sizeof(h), cudaMemcpyDeviceToHost, st));
+  SINKSLOT_CUDA_TRY(cudaStreamSynchronize(st));
+  float f0, f1;
+  memcpy(&f0, &h[0], 4);
+  memcpy(&f1, &h[1], 4);
+  *a0 = (double)f0;
+  *a1 = (double)f1;
+  return kOk;
+}
+
+static double py_max(double a, double b) { return (b > a) ? b : a; }  // Python's max(a, b)
+
+size_t solve_work_floats(int64_t n, int64_t m) { return (size_t)(2 * (n + m) + 64); }
+
+int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t work_floats,
+               int64_t* iters_run, int* converged, double* final_viol, cudaStream_t st) {
+  const int64_t n = sp.row.nseg, m = sp.col.nseg;
+  SINKSLOT_REQUIRE(sp.variant == 0 || sp.variant == 1, "solve: variant must be 0 or 1");
+  SINKSLOT_REQUIRE(sp.mode >= 0 && sp.mode <= 2, "unknown stop.mode");
+  SINKSLOT_REQUIRE(sp.mode == 0 || sp.check_every >= 1, "solve: check_every must be >= 1");
+  SINKSLOT_REQUIRE(work_floats >= (int64_t)solve_work_floats(n, m), "solve: work buffer too small");
+  float* phi_next = work;
+  float* psi_next = work + n;
+  float* prev_phi = work + n + m;
+  float* prev_psi = work + 2 * n + m;
+  uint32_t* acc = reinterpret_cast<uint32_t*>(work + 2 * (n + m));
+  SINKSLOT_CUDA_TRY(cudaMemsetAsync(phi, 0, n * sizeof(float), st));
+  SINKSLOT_CUDA_TRY(cudaMemsetAsync(psi, 0, m * sizeof(float), st));
+  if (sp.mode == 1) {
+    SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_phi, 0, n * sizeof(float), st));
+    SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_psi, 0, m * sizeof(float), st));
+  }
+  const float w_old = (float)(1.0 - sp.alpha), w_new = (float)sp.alpha;
+
+  float* phi_cur = phi;
+  float* psi_cur = psi;
+  float* phi_nx = phi_next;
+  float* psi_nx = psi_next;
+
+  auto row_step = [&](int out_mode, int chk) {
+    HalfStep h = sp.row;
+    h.other = psi_cur;
+    h.base = sp.log_a;
+    h.prev = prev_phi;
+    h.acc = acc;
+    h.w_old = w_old;
+    h.w_new = w_new;
+    if (sp.variant == 0) {  // Gauss-Seidel: in place
+      h.self_old = phi_cur;
+      h.out = phi_cur;
+    } else {
+      h.self_old = phi_cur;
+      h.out = phi_nx;
+    }
+    return half_step(h, out_mode, chk, st);
+  };
+  auto col_step = [&](int out_mode, int chk) {
+    HalfStep h = sp.col;
+    h.other = phi_cur;
+    h.base = sp.log_b;
+    h.prev = prev_psi;
+    h.acc = acc + 1;
+    h.w_old = w_old;
+    h.w_new = w_new;
+    if (sp.variant == 0) {
+      h.self_old = psi_cur;
+      h.out = psi_cur;
+    } else {
+      h.self_old = psi_cur;
+      h.out = psi_nx;
+    }
+    return half_step(h, out_mode, chk, st);
+  };
+  auto swap_sym = [&]() {
+    float* t = phi_cur; phi_cur = phi_nx; phi_nx = t;
+    t = psi_cur; psi_cur = psi_nx; psi_nx = t;
+  };
+  const int step_out = sp.variant == 0 ? kOutPlain : kOutBlend;
+
+  int64_t it = 0;
+  *converged = -1;
+  *final_viol = NAN;
+  if (sp.mode == 0) {
+    for (it = 0; it < sp.n_iters; ++it) {
+      SINKSLOT_TRY(row_step(step_out, kChkNone));
+      SINKSLOT_TRY(col_step(step_out, kChkNone));
+      if (sp.variant == 1) swap_sym();
+    }
+    it = sp.n_iters < 0 ? 0 : sp.n_iters;
+  } else if (sp.mode == 1) {
+    double change = INFINITY;
+    *converged = 0;
+    const double thr = sp.variant == 0 ? sp.tol : sp.alpha * sp.tol;
+    while (it < sp.max_iter) {
+      const bool chk = ((it + 1) % sp.check_every) == 0;
+      if (chk) SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, 2 * sizeof(uint32_t), st));
+      SINKSLOT_TRY(row_step(step_out, chk ? kChkPot : kChkNone));
+      SINKSLOT_TRY(col_step(step_out, chk ? kChkPot : kChkNone));
+      if (sp.variant == 1) swap_sym();
+      ++it;
+      if (chk) {
+        double c0, c1;
+        SINKSLOT_TRY(read_acc(acc, &c0, &c1, st));
+        change = sp.eps * py_max(c0, c1);
+        if (change < thr) {
+          *converged = 1;
+          break;
+        }
+      }
+    }
+    *final_viol = change;
+  } else {
+    double v = INFINITY;
+    *converged = 0;
+    while (it < sp.max_iter) {
+      const bool chk = ((it + 1) % sp.check_every) == 0 || (it + 1) == sp.max_iter;
+      if (chk) SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, 2 * sizeof(uint32_t), st));
+      if (sp.variant == 0) {
+        SINKSLOT_TRY(row_step(kOutPlain, chk ? kChkMarg : kChkNone));
+        SINKSLOT_TRY(col_step(kOutPlain, chk ? kChkMarg : kChkNone));
+      } else {
+        SINKSLOT_TRY(row_step(kOutBlend, kChkNone));
+        SINKSLOT_TRY(col_step(kOutBlend, kChkNone));
+        swap_sym();
+        if (chk) {
+          SINKSLOT_TRY(row_step(kOutNone, kChkMarg));
+          SINKSLOT_TRY(col_step(kOutNone, kChkMarg));
+        }
+      }
+      ++it;
+      if (chk) {
+        double c0, c1;
+        SINKSLOT_TRY(read_acc(acc, &c0, &c1, st));
+        // torch.maximum propagates NaN
+        v = (std::isnan(c0) || std::isnan(c1)) ? NAN : (c0 > c1 ? c0 : c1);
+        if (v <= sp.tol) {
+          *converged = 1;
+          break;
+        }
+      }
+    }
+    *final_viol = v;
+  }
+  if (phi_cur != phi)
+    SINKSLOT_CUDA_TRY(cudaMemcpyAsync(phi, phi_cur, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  if (psi_cur != psi)
+    SINKSLOT_CUDA_TRY(cudaMemcpyAsync(psi, psi_cur, m * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  *iters_run = it;
+  return kOk;
+}
+
+}  // namespace sinkslot

@@ -1,0 +1,166 @@
+"""The fused segmented-LSE half-step and the solve loops on the GPU, against the
+oracle (same support, fp32 torch-backend semantics) and against the
+reference's torch-backend op sequence on the same device.
+
+Tolerance for potentials after a fixed number of iterations: rtol 1e-4,
+atol 1e-5 (fp32).  Early-stopping runs: iteration count within one check
+interval, the same convergence flag, potentials equal up to the (+c, -c)
+shift that Sinkhorn leaves undamped, within 5e-3.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES, assert_close_np, load_golden
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-4, 1e-5
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    torch.backends.cuda.matmul.allow_tf32 = False
+    import sinkslot_b200
+    sinkslot_b200.load_library()
+    return torch.device("cuda:0")
+
+
+def _random_csr(nseg, lens, maxidx, seed, idx_dtype):
+    g = torch.Generator().manual_seed(seed)
+    counts = torch.tensor(lens)[torch.randint(0, len(lens), (nseg,), generator=g)]
+    ptr = torch.zeros(nseg + 1, dtype=torch.int64)
+    ptr[1:] = torch.cumsum(counts, 0)
+    nnz = int(ptr[-1])
+    idx = torch.randint(0, maxidx, (nnz,), generator=g)
+    lam = torch.randn(nnz, generator=g) * 10.0
+    return ptr, idx, lam, nnz, counts
+
+
+@pytest.mark.parametrize("lens,maxidx,idx_dtype", [
+    ([0, 1, 3, 7, 64], 1000, torch.int16),
+    ([60, 64], 1 << 20, torch.int32),
+    ([100, 250, 257, 1000], 5000, torch.int16),
+    ([1, 2], 1 << 16, torch.int32),
+])
+@pytest.mark.parametrize("with_base", [True, False])
+def test_seg_lse_matches_oracle(cuda, oracle, lens, maxidx, idx_dtype, with_base):
+    from sinkslot_b200 import seg_lse_online
+    nseg = 3000
+    ptr, idx, lam, nnz, counts = _random_csr(nseg, lens, maxidx, 5, idx_dtype)
+    g = torch.Generator().manual_seed(6)
+    other = torch.randn(maxidx, generator=g) * 5.0
+    base = torch.randn(nseg, generator=g) if with_base else None
+    zero = torch.zeros(nseg)
+    out = seg_lse_online(ptr.int().to(cuda), idx.to(idx_dtype).to(cuda), lam.to(cuda),
+                         zero.to(cuda), other.to(cuda), nseg,
+                         base=base.to(cuda) if with_base else None)
+    seg = torch.repeat_interleave(torch.arange(nseg), counts)
+    want = oracle.seg_lse_coo(seg.numpy(), idx.numpy(), lam.numpy(), other.numpy(),
+                              base.numpy() if with_base else np.zeros(nseg, np.float32), nseg)
+    if not with_base:
+        want = -want  # oracle computes base - LSE
+    assert_close_np(out.cpu().numpy(), want, rtol=1e-6, atol=2e-5, name="seg_lse")
+
+
+def _gpu_inputs(g, cuda):
+    return [torch.from_numpy(g[k]).to(cuda) for k in ("x", "y", "a", "b")]
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+@pytest.mark.parametrize("variant", ["alternating", "symmetric"])
+def test_fixed_solve_matches_oracle(cuda, oracle, case, variant):
+    from sinkslot_b200 import sinkslot_solve
+    meta, g = load_golden(case)
+    res = sinkslot_solve(*_gpu_inputs(g, cuda), meta["eps"], meta["L"], 0, meta["n_iters"],
+                         variant=variant)
+    assert res.iters_run == meta["n_iters"] and res.converged is None and res.final_viol is None
+    o = oracle.sinkslot_solve(g["x"], g["y"], g["a"], g["b"], meta["eps"], meta["L"], 0,
+                              meta["n_iters"], variant=variant, builder="cuda")
+    np.testing.assert_array_equal(res.rows.cpu().numpy(), o.rows)
+    assert_close_np(res.phi.cpu().numpy(), o.phi, RTOL, ATOL, "phi")
+    assert_close_np(res.psi.cpu().numpy(), o.psi, RTOL, ATOL, "psi")
+    # against the reference's own CPU run when its support is the same
+    key = "alt" if variant == "alternating" else "sym"
+    if "rows_cudabuilder" in g and np.array_equal(o.rows, g["rows_cudabuilder"]) and \
+            np.array_equal(o.cols, g["cols_cudabuilder"]):
+        assert_close_np(res.phi.cpu().numpy(), g[f"phi_{key}"], RTOL, ATOL, "phi vs reference")
+        assert_close_np(res.psi.cpu().numpy(), g[f"psi_{key}"], RTOL, ATOL, "psi vs reference")
+
+
+@pytest.mark.parametrize("variant", ["alternating", "symmetric"])
+@pytest.mark.parametrize("mode,tol,every", [("marginal", 1e-6, 5), ("potential", 1e-4, 5),
+                                            ("marginal", 1e-5, 7)])
+def test_stop_modes_match_oracle(cuda, oracle, variant, mode, tol, every):
+    from sinkslot_b200 import sinkslot_solve
+    meta, g = load_golden("small_nonuniform")
+    res = sinkslot_solve(*_gpu_inputs(g, cuda), meta["eps"], meta["L"], 0, 20000,
+                         stop_mode=mode, stop_max_iter=20000, stop_tol=tol,
+                         stop_check_every=every, variant=variant)
+    o = oracle.sinkslot_solve(g["x"], g["y"], g["a"], g["b"], meta["eps"], meta["L"], 0, 20000,
+                              stop_mode=mode, stop_max_iter=20000, stop_tol=tol,
+                              stop_check_every=every, variant=variant, builder="cuda")
+    assert res.converged == o.converged
+    assert abs(res.iters_run - o.iters_run) <= every
+    assert res.iters_run % every == 0
+    c = float((res.phi.cpu().double() - torch.from_numpy(o.phi).double()).mean())
+    np.testing.assert_allclose(res.phi.cpu().numpy() - c, o.phi, rtol=0, atol=5e-3)
+    np.testing.assert_allclose(res.psi.cpu().numpy() + c, o.psi, rtol=0, atol=5e-3)
+    if mode == "marginal":
+        assert res.final_viol <= tol
+    else:
+        assert res.final_viol < (tol if variant == "alternating" else 0.5 * tol)
+
+
+def test_max_iter_cap_and_final_check(cuda):
+    """marginal mode checks at it == max_iter too; potential mode does not."""
+    from sinkslot_b200 import sinkslot_solve
+    meta, g = load_golden("small_nonuniform")
+    t = _gpu_inputs(g, cuda)
+    r = sinkslot_solve(*t, 0.05, 40, 0, 10, stop_mode="marginal", stop_max_iter=7,
+                       stop_tol=1e-12, stop_check_every=5)
+    assert r.iters_run == 7 and r.converged is False and np.isfinite(r.final_viol)
+    r = sinkslot_solve(*t, 0.05, 40, 0, 10, stop_mode="potential", stop_max_iter=4,
+                       stop_tol=1e-12, stop_check_every=5)
+    assert r.iters_run == 4 and r.converged is False and r.final_viol == float("inf")
+
+
+def test_full_size_alternating_matches_torch_reference_ops(cuda):
+    """N = M = 2^20, d = 3, L = 64, eps = 0.01, 500 alternating iterations: the
+    fused loop against the reference torch backend's op sequence on the same
+    device and support."""
+    from oracle.torch_ref import alternating_fixed
+    from sinkslot_b200 import sinkslot_solve
+    from sinkslot_b200.solver import cost_and_lam
+    torch.manual_seed(1)
+    n = 1 << 20
+    X = torch.randn(n, 3).to(cuda)
+    Y = (torch.randn(n, 3) + 1.5).to(cuda)
+    a = torch.full((n,), 1.0 / n, device=cuda)
+    res = sinkslot_solve(X, Y, a, a, 0.01, 64, 0, 500)
+    lam, _ = cost_and_lam(X, Y, res.rows, res.cols, res.S, 0.01)
+    phi, psi = alternating_fixed(res.rows, res.cols, lam, a.log(), a.log(), n, n, 500)
+    d_phi = (res.phi - phi).abs()
+    bad = d_phi > ATOL + RTOL * phi.abs()
+    assert int(bad.sum()) == 0, f"{int(bad.sum())} phi outside tol, max {float(d_phi.max()):.3e}"
+    d_psi = (res.psi - psi).abs()
+    bad = d_psi > ATOL + RTOL * psi.abs()
+    assert int(bad.sum()) == 0, f"{int(bad.sum())} psi outside tol, max {float(d_psi.max()):.3e}"
+    # column marginal is exact after the column half-step (size-independent property)
+    P = (res.phi[res.rows] + res.psi[res.cols] + lam).exp()
+    col = torch.zeros(n, device=cuda, dtype=torch.float64).index_add_(0, res.cols, P.double())
+    torch.testing.assert_close(col, a.double(), rtol=1e-4, atol=0)
+
+
+def test_deterministic_and_auto_equals_b200(cuda):
+    from sinkslot_b200 import sinkslot_solve
+    meta, g = load_golden("bench_shape")
+    t = _gpu_inputs(g, cuda)
+    r1 = sinkslot_solve(*t, 0.05, 32, 0, 100, backend="auto")
+    r2 = sinkslot_solve(*t, 0.05, 32, 0, 100, backend="b200")
+    assert torch.equal(r1.phi, r2.phi) and torch.equal(r1.psi, r2.psi)
+    assert torch.equal(r1.S, r2.S)
