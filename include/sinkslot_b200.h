@@ -59,15 +59,19 @@ int sinkslot_support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chu
                                      int64_t* bytes_host);
 
 /* Sliced-lifted support: replaces `sot_plan_coo(X, Y, a, b, L, seed, chunk,
- * ot1d=_ot_1d_coo_batched_cuda)`, sinkslot/solver.py:153-232.  theta (L, d)
- * fp32 on the device holds get_random_projections(d, L, seed) cast to fp32
- * (solver.py:193).  chunk <= 0 means all L slices in one batch.  The coalesced
- * support stays in the workspace; *nnz_host receives its size.  Call
- * sinkslot_support_export with the same sizes to read it out. */
+ * ot1d=_ot_1d_coo_batched_cuda)`, sinkslot/solver.py:153-232.  The
+ * projections come either from PX (n, L) / PY (m, L), row-major -- the
+ * reference's `X @ th.T` per chunk (solver.py:221), computed by the caller's
+ * GEMM so their bits are the reference's -- or, when PX and PY are NULL, from
+ * theta (L, d) fp32 (get_random_projections(d, L, seed) cast to fp32,
+ * solver.py:193) as the sequential FMA chain over d.  chunk <= 0 means all L
+ * slices in one batch.  The coalesced support stays in the workspace;
+ * *nnz_host receives its size.  Call sinkslot_support_export with the same
+ * sizes to read it out. */
 int sinkslot_build_support(const float* X, const float* Y, const float* a, const float* b,
-                           int64_t n, int64_t m, int d, const float* theta, int L, int chunk,
-                           void* workspace, int64_t workspace_bytes, int64_t* nnz_host,
-                           void* stream);
+                           int64_t n, int64_t m, int d, const float* theta, const float* PX,
+                           const float* PY, int L, int chunk, void* workspace,
+                           int64_t workspace_bytes, int64_t* nnz_host, void* stream);
 
 /* rows, cols (int64) and S (fp32) of the support built by
  * sinkslot_build_support, sorted by rows * m + cols: the return value of
@@ -118,20 +122,47 @@ int sinkslot_seg_lse(const int32_t* indptr, const void* idx, int idx_bytes, cons
 /* Scratch floats sinkslot_solve_csr needs for an (n, m) problem. */
 int sinkslot_solve_work_floats(int64_t n, int64_t m, int64_t* floats_host);
 
+/* Bytes of the column-blocked layout of one CSR side (nseg segments gathering
+ * from a potential of length m_other) and of the scratch its builder needs.
+ * The geometry follows the current device's SM count: build and solve on the
+ * same device model. */
+int sinkslot_tiles_bytes(int64_t nseg, int64_t m_other, int64_t nnz, int64_t* layout_bytes_host,
+                         int64_t* build_bytes_host);
+
+/* The tiled layout's geometry: geom_host[0..4] = panels P, rows per panel R,
+ * column blocks B, log2 of the block width W, dynamic shared memory bytes.
+ * Layout bytes: int64 header[8] | int64 tile_start[P*B + 1] | uint32 meta[nnz]
+ * (row within panel << 16 | column within block) | float lam[nnz], each part
+ * 256-byte aligned; tile t = p*B + b holds entries [tile_start[t],
+ * tile_start[t+1]) in CSR order. */
+int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geom_host);
+
+/* Column-blocked layout of a CSR side for the shared-memory-staged half-step
+ * (no counterpart in the reference: a layout of its CSR, `to_csr`,
+ * sinkslot/solver.py:235-276, built once per solve). */
+int sinkslot_build_tiles(const int32_t* indptr, const void* idx, int idx_bytes, const float* lam,
+                         int64_t nseg, int64_t m_other, int64_t nnz, void* layout,
+                         int64_t layout_bytes, void* workspace, int64_t workspace_bytes,
+                         void* stream);
+
 /* Full Sinkhorn loop over prebuilt CSR (rows) / CSC (cols): replaces
  * `sinkslot_alternating_triton` (variant 0) and `sinkslot_symmetric_triton`
  * (variant 1), sinkslot/sinkhorn_solvers.py:195-419, with the semantics of
  * their torch twins (:443-588).  stop_mode: 0 fixed (n_iters), 1 potential,
- * 2 marginal (up to max_iter, checked every check_every).  phi (n), psi (m)
- * receive the absorbed potentials.  *converged_host: -1 (fixed mode), 0 or 1;
- * *final_viol_host: NaN in fixed mode. */
+ * 2 marginal (up to max_iter, checked every check_every).  r_tiles / c_tiles
+ * (both or neither) are layouts from sinkslot_build_tiles of the two sides;
+ * with them every iteration after the first runs the shared-memory-staged
+ * half-step.  phi (n), psi (m) receive the absorbed potentials.
+ * *converged_host: -1 (fixed mode), 0 or 1; *final_viol_host: NaN in fixed
+ * mode. */
 int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                        const float* r_lam, const int32_t* c_ptr, const void* c_idx,
                        int c_idx_bytes, const float* c_lam, int64_t nnz, const float* log_a,
                        const float* log_b, int64_t n, int64_t m, int variant, int stop_mode,
                        int64_t n_iters, int64_t max_iter, int64_t check_every, double tol,
-                       double eps, double alpha, float* phi, float* psi, float* work,
-                       int64_t work_floats, int64_t* iters_host, int* converged_host,
+                       double eps, double alpha, const void* r_tiles, int64_t r_tiles_bytes,
+                       const void* c_tiles, int64_t c_tiles_bytes, float* phi, float* psi,
+                       float* work, int64_t work_floats, int64_t* iters_host, int* converged_host,
                        double* final_viol_host, void* stream);
 
 /* ---------------------------------------------------------------------------
@@ -147,7 +178,8 @@ int sinkslot_plan_values(const float* phi, const float* psi, const int64_t* rows
                          const int64_t* cols, const float* S, const float* x, const float* y,
                          int d, int64_t nnz, double eps, int grad_form, float* out, void* stream);
 
-int sinkslot_barycentric_workspace_bytes(int64_t n, int64_t m, int d, int64_t* bytes_host);
+int sinkslot_barycentric_workspace_bytes(int64_t nnz, int64_t n, int64_t m, int d,
+                                         int64_t* bytes_host);
 
 /* Barycentric projections of a sparse plan and the envelope gradient:
  * replaces `sparse_barycentric_map(T_vals, rows, cols, x, y)` (sinkslot/gradient.py:25-61)

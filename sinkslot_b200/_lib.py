@@ -34,8 +34,8 @@ _SIGNATURES = {
     "sinkslot_ot1d_batched": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_i64, c_vp, c_vp,
                               c_vp, c_vp, c_vp, c_vp, c_vp, P_i64, c_vp],
     "sinkslot_support_workspace_bytes": [c_i64, c_i64, c_int, c_int, c_int, P_i64],
-    "sinkslot_build_support": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_int, c_int,
-                               c_vp, c_i64, P_i64, c_vp],
+    "sinkslot_build_support": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_vp, c_vp,
+                               c_int, c_int, c_vp, c_i64, P_i64, c_vp],
     "sinkslot_support_export": [c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, c_i64, c_vp, c_vp,
                                 c_vp, c_vp],
     "sinkslot_csr_workspace_bytes": [c_i64, c_i64, P_i64],
@@ -47,10 +47,15 @@ _SIGNATURES = {
     "sinkslot_solve_work_floats": [c_i64, c_i64, P_i64],
     "sinkslot_solve_csr": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_vp, c_vp,
                            c_i64, c_i64, c_int, c_int, c_i64, c_i64, c_i64, c_dbl, c_dbl, c_dbl,
+                           c_vp, c_i64, c_vp, c_i64,
                            c_vp, c_vp, c_vp, c_i64, P_i64, P_int, P_dbl, c_vp],
+    "sinkslot_tiles_bytes": [c_i64, c_i64, c_i64, P_i64, P_i64],
+    "sinkslot_tiles_geometry": [c_i64, c_i64, c_i64, P_int],
+    "sinkslot_build_tiles": [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp,
+                             c_i64, c_vp],
     "sinkslot_plan_values": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_dbl, c_int,
                              c_vp, c_vp],
-    "sinkslot_barycentric_workspace_bytes": [c_i64, c_i64, c_int, P_i64],
+    "sinkslot_barycentric_workspace_bytes": [c_i64, c_i64, c_i64, c_int, P_i64],
     "sinkslot_barycentric": [c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_vp,
                              c_vp, c_vp, c_vp, c_i64, c_vp],
     "sinkslot_dual_value": [c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp],

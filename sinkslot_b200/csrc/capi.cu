@@ -69,14 +69,14 @@ int sinkslot_support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chu
 }
 
 int sinkslot_build_support(const float* X, const float* Y, const float* a, const float* b,
-                           int64_t n, int64_t m, int d, const float* theta, int L, int chunk,
-                           void* workspace, int64_t workspace_bytes, int64_t* nnz_host,
-                           void* stream) {
+                           int64_t n, int64_t m, int d, const float* theta, const float* PX,
+                           const float* PY, int L, int chunk, void* workspace,
+                           int64_t workspace_bytes, int64_t* nnz_host, void* stream) {
   g_last_error_clear();
-  SINKSLOT_REQUIRE(X && Y && a && b && theta && workspace && nnz_host,
+  SINKSLOT_REQUIRE(a && b && workspace && nnz_host && ((X && Y && theta) || (PX && PY)),
                    "build_support: null argument");
-  return build_support(X, Y, a, b, n, m, d, theta, L, chunk, workspace, (size_t)workspace_bytes,
-                       nnz_host, ST(stream));
+  return build_support(X, Y, a, b, n, m, d, theta, PX, PY, L, chunk, workspace,
+                       (size_t)workspace_bytes, nnz_host, ST(stream));
 }
 
 int sinkslot_support_export(const void* workspace, int64_t workspace_bytes, int64_t n, int64_t m,
@@ -155,8 +155,9 @@ int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                        int c_idx_bytes, const float* c_lam, int64_t nnz, const float* log_a,
                        const float* log_b, int64_t n, int64_t m, int variant, int stop_mode,
                        int64_t n_iters, int64_t max_iter, int64_t check_every, double tol,
-                       double eps, double alpha, float* phi, float* psi, float* work,
-                       int64_t work_floats, int64_t* iters_host, int* converged_host,
+                       double eps, double alpha, const void* r_tiles, int64_t r_tiles_bytes,
+                       const void* c_tiles, int64_t c_tiles_bytes, float* phi, float* psi,
+                       float* work, int64_t work_floats, int64_t* iters_host, int* converged_host,
                        double* final_viol_host, void* stream) {
   g_last_error_clear();
   SINKSLOT_REQUIRE(r_ptr && c_ptr && log_a && log_b && phi && psi && work && iters_host &&
@@ -164,6 +165,16 @@ int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                    "solve_csr: null argument");
   SINKSLOT_REQUIRE(nnz == 0 || (r_idx && r_lam && c_idx && c_lam), "solve_csr: null argument");
   SolveSpec sp;
+  if (r_tiles || c_tiles) {
+    SINKSLOT_REQUIRE(r_tiles && c_tiles, "solve_csr: give both tiled layouts or neither");
+    sp.row_geom = tile_geom(n, m, nnz, num_sms());
+    sp.col_geom = tile_geom(m, n, nnz, num_sms());
+    SINKSLOT_REQUIRE(r_tiles_bytes >= (int64_t)sp.row_geom.layout_bytes &&
+                         c_tiles_bytes >= (int64_t)sp.col_geom.layout_bytes,
+                     "solve_csr: tiled layout buffer too small");
+    sp.row_tiles = r_tiles;
+    sp.col_tiles = c_tiles;
+  }
   sp.row.ptr = r_ptr;
   sp.row.idx = r_idx;
   sp.row.idx_bytes = r_idx_bytes;
@@ -190,6 +201,44 @@ int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                     ST(stream));
 }
 
+int sinkslot_tiles_bytes(int64_t nseg, int64_t m_other, int64_t nnz, int64_t* layout_bytes_host,
+                         int64_t* build_bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(layout_bytes_host && build_bytes_host && nseg >= 1 && m_other >= 1 && nnz >= 0,
+                   "tiles_bytes: bad args");
+  const TileGeom g = tile_geom(nseg, m_other, nnz, num_sms());
+  *layout_bytes_host = (int64_t)g.layout_bytes;
+  *build_bytes_host = (int64_t)g.build_bytes;
+  return kOk;
+}
+
+int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geom_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(geom_host && nseg >= 1 && m_other >= 1 && nnz >= 0, "tiles_geometry: bad args");
+  const TileGeom g = tile_geom(nseg, m_other, nnz, num_sms());
+  geom_host[0] = g.P;
+  geom_host[1] = g.R;
+  geom_host[2] = g.B;
+  geom_host[3] = g.logW;
+  geom_host[4] = (int)g.smem_bytes;
+  return kOk;
+}
+
+int sinkslot_build_tiles(const int32_t* indptr, const void* idx, int idx_bytes, const float* lam,
+                         int64_t nseg, int64_t m_other, int64_t nnz, void* layout,
+                         int64_t layout_bytes, void* workspace, int64_t workspace_bytes,
+                         void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(indptr && layout && workspace && (nnz == 0 || (idx && lam)),
+                   "build_tiles: null argument");
+  SINKSLOT_REQUIRE(nseg >= 1 && m_other >= 1 && nnz >= 0, "build_tiles: bad sizes");
+  const TileGeom g = tile_geom(nseg, m_other, nnz, num_sms());
+  SINKSLOT_REQUIRE(layout_bytes >= (int64_t)g.layout_bytes, "build_tiles: layout buffer too small");
+  SINKSLOT_REQUIRE(workspace_bytes >= (int64_t)g.build_bytes, "build_tiles: workspace too small");
+  return build_tiles(indptr, idx, idx_bytes, lam, g, layout, workspace, (size_t)workspace_bytes,
+                     ST(stream));
+}
+
 int sinkslot_plan_values(const float* phi, const float* psi, const int64_t* rows,
                          const int64_t* cols, const float* S, const float* x, const float* y,
                          int d, int64_t nnz, double eps, int grad_form, float* out, void* stream) {
@@ -200,10 +249,12 @@ int sinkslot_plan_values(const float* phi, const float* psi, const int64_t* rows
   return plan_values(phi, psi, rows, cols, S, x, y, d, nnz, eps, grad_form, out, ST(stream));
 }
 
-int sinkslot_barycentric_workspace_bytes(int64_t n, int64_t m, int d, int64_t* bytes_host) {
+int sinkslot_barycentric_workspace_bytes(int64_t nnz, int64_t n, int64_t m, int d,
+                                         int64_t* bytes_host) {
   g_last_error_clear();
-  SINKSLOT_REQUIRE(bytes_host && n >= 0 && m >= 0 && d >= 1, "barycentric_workspace_bytes: bad args");
-  *bytes_host = (int64_t)bary_workspace_bytes(n, m, d);
+  SINKSLOT_REQUIRE(bytes_host && nnz >= 0 && n >= 0 && m >= 0 && d >= 1,
+                   "barycentric_workspace_bytes: bad args");
+  *bytes_host = (int64_t)bary_workspace_bytes(nnz, n, m, d);
   return kOk;
 }
 

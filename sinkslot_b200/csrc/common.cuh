@@ -70,7 +70,7 @@ inline int num_sms() {
 
 __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+__host__ __device__ inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 
 // Bump allocator over a caller-provided workspace.  Every carve is 256-byte
 // aligned; `ok` turns false when the workspace is too small.
@@ -82,7 +82,7 @@ struct Carver {
   Carver(void* p, size_t c) : base(static_cast<char*>(p)), cap(c) {}
   template <typename T>
   T* take(size_t count) {
-    size_t bytes = align_up(count * sizeof(T) + 1);
+    size_t bytes = align_up(count > 0 ? count * sizeof(T) : 1);
     if (used + bytes > cap) {
       ok = false;
       used += bytes;

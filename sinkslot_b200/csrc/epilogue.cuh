@@ -1,0 +1,51 @@
+// epilogue.cuh -- what a half-step does with one segment's log-sum-exp:
+// res = base - lse (lse itself without base), then the write mode and the
+// stop-criterion contribution.  Shared by the exact and the tiled half-steps so
+// both produce the same bits for the same lse.
+#pragma once
+
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace sinkslot {
+
+enum OutMode { kOutPlain = 0, kOutBlend = 1, kOutNone = 2 };
+enum CheckMode { kChkNone = 0, kChkMarg = 1, kChkPot = 2 };
+
+// sinkhorn_solvers.py: the reference's `base - LSE` (:91-93), the symmetric
+// blend `(1 - alpha) * x + alpha * cand` (:361-363), the marginal proxy
+// `|a * exp(old - new) - a|` (:280-283, :405-412) and the potential change
+// `|new - prev|` (:250-254).
+template <int OUT, int CHK>
+__device__ __forceinline__ void segment_epilogue(int64_t seg, float lse, const float* base,
+                                                 const float* self_old, float* out, float w_old,
+                                                 float w_new, float* prev, uint32_t& chk_bits) {
+  const float b = base ? base[seg] : 0.0f;
+  const float res = base ? __fsub_rn(b, lse) : lse;
+  float nv = res;
+  float old = 0.0f;
+  if (OUT == kOutBlend || CHK == kChkMarg) old = self_old[seg];
+  if (OUT == kOutBlend) nv = __fadd_rn(__fmul_rn(w_old, old), __fmul_rn(w_new, res));
+  if (OUT != kOutNone) out[seg] = nv;
+  if (CHK == kChkMarg) {
+    const float ea = expf(b);
+    const float t = __fmul_rn(ea, expf(__fsub_rn(old, res)));
+    chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(t, ea)));
+  } else if (CHK == kChkPot) {
+    chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(nv, prev[seg])));
+    prev[seg] = nv;
+  }
+}
+
+template <int CHK>
+__device__ __forceinline__ void check_reduce(uint32_t chk_bits, uint32_t* acc) {
+  if (CHK != kChkNone) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1)
+      chk_bits = max(chk_bits, __shfl_xor_sync(0xffffffffu, chk_bits, o));
+    if ((threadIdx.x & 31) == 0 && chk_bits) atomicMax(acc, chk_bits);
+  }
+}
+
+}  // namespace sinkslot

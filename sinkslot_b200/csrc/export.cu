@@ -5,14 +5,15 @@
 //                       sub / square / sum), lam = log(max(S, tiny)) - cost / eps
 //   plan_values_kernel  sinkhorn_solvers.py:757-758 (plan) and gradient.py:95-97
 //                       (T_vals): exp of the potentials plus lam, cost recomputed
-//   bary_rows_kernel    gradient.py:52-59 for row-sorted COO: per-row sums in COO
-//                       order (the order of the reference's CPU index_add_), then
+//   seg_bary_kernel     gradient.py:52-59: per-row (and per-column) sums of the
+//                       plan in COO order -- the order of the reference's CPU
+//                       index_add_, so results are deterministic -- then
 //                       Tx = sum(T y) / max(sum T, tiny) and grad = 2 a (x - Tx)
-//   bary_atomic_kernel  the same sums for unsorted COO and for the column side
 #include <cfloat>
 
 #include "common.cuh"
 #include "export.h"
+#include "primitives.h"
 
 namespace sinkslot {
 
@@ -86,21 +87,14 @@ int plan_values(const float* phi, const float* psi, const int64_t* rows, const i
   return kOk;
 }
 
-// row boundaries of a row-sorted COO: ptr[i] = #{rows < i}
-__global__ void row_ptr_kernel(const int64_t* __restrict__ rows, int64_t nnz, int64_t n,
-                               int64_t* __restrict__ ptr) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t lo = 0, hi = nnz;
-    while (lo < hi) {
-      const int64_t mid = (lo + hi) >> 1;
-      if (rows[mid] < i) lo = mid + 1; else hi = mid;
-    }
-    ptr[i] = lo;
-  }
-}
+// Per-segment sums of a sparse plan in COO order (the order of the reference's
+// CPU index_add_): the entries are grouped by `seg` with a stable sort (skipped
+// when `seg` is already non-decreasing), then one thread per segment sums
+//   tot = sum T,  acc_j = sum T * pts[oth, j]
+// and writes Tout = acc / max(tot, tiny) and, optionally, grad = 2 a (x - Tout).
+constexpr int kMaxD = 16;
 
-__global__ void rows_sorted_kernel(const int64_t* __restrict__ r, int64_t nnz, int* flag) {
+__global__ void seg_sorted_check_kernel(const int64_t* __restrict__ r, int64_t nnz, int* flag) {
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x + 1; k < nnz;
        k += (int64_t)gridDim.x * blockDim.x)
     if (r[k] < r[k - 1]) {
@@ -109,68 +103,112 @@ __global__ void rows_sorted_kernel(const int64_t* __restrict__ r, int64_t nnz, i
     }
 }
 
-constexpr int kMaxD = 16;
+__global__ void seg_key32_kernel(const int64_t* __restrict__ r, int64_t nnz,
+                                 uint32_t* __restrict__ k) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
+       q += (int64_t)gridDim.x * blockDim.x)
+    k[q] = (uint32_t)r[q];
+}
 
-__global__ void bary_rows_kernel(const float* __restrict__ T, const int64_t* __restrict__ cols,
-                                 const int64_t* __restrict__ ptr, const float* __restrict__ x,
-                                 const float* __restrict__ y, int64_t n, int d,
-                                 const float* __restrict__ a, float* __restrict__ Tx,
-                                 float* __restrict__ grad) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+// ptr[i] = #{keys < i} over sorted keys (int64 COO indices or uint32 sort keys)
+template <typename KT>
+__global__ void seg_ptr_kernel(const KT* __restrict__ keys, int64_t nnz, int64_t nseg,
+                               int64_t* __restrict__ ptr) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= nseg;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t lo = 0, hi = nnz;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if ((int64_t)keys[mid] < i) lo = mid + 1; else hi = mid;
+    }
+    ptr[i] = lo;
+  }
+}
+
+__global__ void seg_bary_kernel(const float* __restrict__ T, const int64_t* __restrict__ oth,
+                                const uint32_t* __restrict__ perm, const int64_t* __restrict__ ptr,
+                                const float* __restrict__ pts, int64_t nseg, int d,
+                                const float* __restrict__ self_pts, const float* __restrict__ a,
+                                float* __restrict__ Tout, float* __restrict__ grad) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nseg;
        i += (int64_t)gridDim.x * blockDim.x) {
     float acc[kMaxD];
     for (int j = 0; j < d; ++j) acc[j] = 0.0f;
-    float r = 0.0f;
-    for (int64_t k = ptr[i]; k < ptr[i + 1]; ++k) {
+    float tot = 0.0f;
+    for (int64_t q = ptr[i]; q < ptr[i + 1]; ++q) {
+      const int64_t k = perm ? (int64_t)perm[q] : q;
       const float t = T[k];
-      const float* yc = y + cols[k] * d;
-      r = __fadd_rn(r, t);
-      for (int j = 0; j < d; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(t, yc[j]));
+      const float* p = pts + oth[k] * d;
+      tot = __fadd_rn(tot, t);
+      for (int j = 0; j < d; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(t, p[j]));
     }
-    const float den = fmaxf(r, FLT_MIN);
+    const float den = fmaxf(tot, FLT_MIN);
     for (int j = 0; j < d; ++j) {
       const float tx = __fdiv_rn(acc[j], den);
-      if (Tx) Tx[i * d + j] = tx;
-      if (grad) grad[i * d + j] = __fmul_rn(__fmul_rn(2.0f, a[i]), __fsub_rn(x[i * d + j], tx));
+      if (Tout) Tout[i * d + j] = tx;
+      if (grad)
+        grad[i * d + j] = __fmul_rn(__fmul_rn(2.0f, a[i]), __fsub_rn(self_pts[i * d + j], tx));
     }
   }
 }
 
-// accumulate sums for one side with atomics: tot[seg] += T, acc[seg, j] += T * pts[other, j]
-__global__ void bary_atomic_kernel(const float* __restrict__ T, const int64_t* __restrict__ seg,
-                                   const int64_t* __restrict__ oth, const float* __restrict__ pts,
-                                   int64_t nnz, int d, float* __restrict__ tot,
-                                   float* __restrict__ acc) {
-  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nnz;
-       k += (int64_t)gridDim.x * blockDim.x) {
-    const float t = T[k];
-    const int64_t s = seg[k];
-    const float* p = pts + oth[k] * d;
-    atomicAdd(tot + s, t);
-    for (int j = 0; j < d; ++j) atomicAdd(acc + s * d + j, __fmul_rn(t, p[j]));
-  }
+struct BaryWs {
+  uint32_t *k1, *v1, *k2, *v2;
+  int64_t *hist, *stmp, *ptr;
+  int* flag;
+};
+
+static void carve_bary(Carver& cv, BaryWs& w, int64_t nnz, int64_t n, int64_t m) {
+  const int64_t e = nnz > 0 ? nnz : 1;
+  w.k1 = cv.take<uint32_t>(e); w.v1 = cv.take<uint32_t>(e);
+  w.k2 = cv.take<uint32_t>(e); w.v2 = cv.take<uint32_t>(e);
+  const int64_t nh = radix_hist_elems(1, e);
+  w.hist = cv.take<int64_t>(nh);
+  w.stmp = cv.take<int64_t>(scan_tmp_elems(nh));
+  w.ptr = cv.take<int64_t>((n > m ? n : m) + 1);
+  w.flag = cv.take<int>(4);
 }
 
-__global__ void bary_finish_kernel(const float* __restrict__ tot, const float* __restrict__ acc,
-                                   const float* __restrict__ x, const float* __restrict__ a,
-                                   int64_t n, int d, float* __restrict__ Tx,
-                                   float* __restrict__ grad) {
-  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n * d;
-       q += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = q / d;
-    const float tx = __fdiv_rn(acc[q], fmaxf(tot[i], FLT_MIN));
-    if (Tx) Tx[q] = tx;
-    if (grad) grad[q] = __fmul_rn(__fmul_rn(2.0f, a[i]), __fsub_rn(x[q], tx));
-  }
-}
-
-size_t bary_workspace_bytes(int64_t n, int64_t m, int d) {
+size_t bary_workspace_bytes(int64_t nnz, int64_t n, int64_t m, int d) {
+  (void)d;
   Carver cv(nullptr, 0);
-  cv.take<int64_t>(n + 1);
-  cv.take<float>(n > m ? n : m);
-  cv.take<float>((n > m ? n : m) * d);
-  cv.take<int>(4);
+  BaryWs w;
+  carve_bary(cv, w, nnz, n, m);
   return cv.used;
+}
+
+static int side_sums(const float* T, const int64_t* seg, const int64_t* oth, int64_t nnz,
+                     const float* pts, int64_t nseg, int d, const float* self_pts, const float* a,
+                     float* Tout, float* grad, BaryWs& w, cudaStream_t st) {
+  int unsorted = 0;
+  if (nnz > 1) {
+    SINKSLOT_CUDA_TRY(cudaMemsetAsync(w.flag, 0, sizeof(int), st));
+    seg_sorted_check_kernel<<<grid_for_e(nnz, 256), 256, 0, st>>>(seg, nnz, w.flag);
+    SINKSLOT_CHECK_LAUNCH();
+    SINKSLOT_CUDA_TRY(cudaMemcpyAsync(&unsorted, w.flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+    SINKSLOT_CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  const uint32_t* perm = nullptr;
+  if (!unsorted) {
+    seg_ptr_kernel<int64_t><<<grid_for_e(nseg + 1, 256), 256, 0, st>>>(seg, nnz, nseg, w.ptr);
+  } else {
+    seg_key32_kernel<<<grid_for_e(nnz, 256), 256, 0, st>>>(seg, nnz, w.k1);
+    SINKSLOT_CHECK_LAUNCH();
+    bool alt = false;
+    SINKSLOT_TRY(radix_sort_pairs<uint32_t>(w.k1, w.v1, w.k2, w.v2, true, 1, nnz,
+                                            bits_for((uint64_t)(nseg > 1 ? nseg : 1)), w.hist,
+                                            w.stmp, &alt, st));
+    perm = alt ? w.v2 : w.v1;
+    seg_ptr_kernel<uint32_t><<<grid_for_e(nseg + 1, 256), 256, 0, st>>>(alt ? w.k2 : w.k1, nnz,
+                                                                        nseg, w.ptr);
+  }
+  SINKSLOT_CHECK_LAUNCH();
+  if (nseg > 0) {
+    seg_bary_kernel<<<grid_for_e(nseg, 128), 128, 0, st>>>(T, oth, perm, w.ptr, pts, nseg, d,
+                                                          self_pts, a, Tout, grad);
+    SINKSLOT_CHECK_LAUNCH();
+  }
+  return kOk;
 }
 
 int barycentric(const float* T, const int64_t* rows, const int64_t* cols, int64_t nnz,
@@ -178,51 +216,19 @@ int barycentric(const float* T, const int64_t* rows, const int64_t* cols, int64_
                 float* Tx, float* Ty, float* grad, void* ws, size_t ws_bytes, cudaStream_t st) {
   SINKSLOT_REQUIRE(d >= 1 && d <= kMaxD, "barycentric: d must be in [1, 16]");
   SINKSLOT_REQUIRE(grad == nullptr || a != nullptr, "barycentric: grad needs a");
+  SINKSLOT_REQUIRE(nnz < (int64_t(1) << 32) && n < (int64_t(1) << 31) && m < (int64_t(1) << 31),
+                   "barycentric: sizes too large");
   Carver cv(ws, ws_bytes);
-  int64_t* ptr = cv.take<int64_t>(n + 1);
-  float* tot = cv.take<float>(n > m ? n : m);
-  float* acc = cv.take<float>((n > m ? n : m) * d);
-  int* flag = cv.take<int>(4);
+  BaryWs w;
+  carve_bary(cv, w, nnz, n, m);
   if (!cv.ok) {
     set_error("barycentric: workspace too small");
     return kWorkspaceTooSmall;
   }
-  int unsorted = 0;
-  if (nnz > 1) {
-    SINKSLOT_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(int), st));
-    rows_sorted_kernel<<<grid_for_e(nnz, 256), 256, 0, st>>>(rows, nnz, flag);
-    SINKSLOT_CHECK_LAUNCH();
-    SINKSLOT_CUDA_TRY(cudaMemcpyAsync(&unsorted, flag, sizeof(int), cudaMemcpyDeviceToHost, st));
-    SINKSLOT_CUDA_TRY(cudaStreamSynchronize(st));
-  }
-  if (Tx || grad) {
-    if (!unsorted) {
-      row_ptr_kernel<<<grid_for_e(n + 1, 256), 256, 0, st>>>(rows, nnz, n, ptr);
-      SINKSLOT_CHECK_LAUNCH();
-      bary_rows_kernel<<<grid_for_e(n, 128), 128, 0, st>>>(T, cols, ptr, x, y, n, d, a, Tx, grad);
-      SINKSLOT_CHECK_LAUNCH();
-    } else {
-      SINKSLOT_CUDA_TRY(cudaMemsetAsync(tot, 0, n * sizeof(float), st));
-      SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, n * d * sizeof(float), st));
-      if (nnz > 0) {
-        bary_atomic_kernel<<<grid_for_e(nnz, 256), 256, 0, st>>>(T, rows, cols, y, nnz, d, tot, acc);
-        SINKSLOT_CHECK_LAUNCH();
-      }
-      bary_finish_kernel<<<grid_for_e(n * d, 256), 256, 0, st>>>(tot, acc, x, a, n, d, Tx, grad);
-      SINKSLOT_CHECK_LAUNCH();
-    }
-  }
-  if (Ty) {
-    SINKSLOT_CUDA_TRY(cudaMemsetAsync(tot, 0, m * sizeof(float), st));
-    SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, m * d * sizeof(float), st));
-    if (nnz > 0) {
-      bary_atomic_kernel<<<grid_for_e(nnz, 256), 256, 0, st>>>(T, cols, rows, x, nnz, d, tot, acc);
-      SINKSLOT_CHECK_LAUNCH();
-    }
-    bary_finish_kernel<<<grid_for_e(m * d, 256), 256, 0, st>>>(tot, acc, nullptr, nullptr, m, d, Ty,
-                                                              nullptr);
-    SINKSLOT_CHECK_LAUNCH();
-  }
+  if (Tx || grad)
+    SINKSLOT_TRY(side_sums(T, rows, cols, nnz, y, n, d, x, a, Tx, grad, w, st));
+  if (Ty)
+    SINKSLOT_TRY(side_sums(T, cols, rows, nnz, x, m, d, nullptr, nullptr, Ty, nullptr, w, st));
   return kOk;
 }
 

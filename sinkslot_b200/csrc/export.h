@@ -11,7 +11,7 @@ int cost_lam(const float* x, const float* y, int d, const int64_t* rows, const i
 int plan_values(const float* phi, const float* psi, const int64_t* rows, const int64_t* cols,
                 const float* S, const float* x, const float* y, int d, int64_t nnz, double eps,
                 int grad_form, float* out, cudaStream_t st);
-size_t bary_workspace_bytes(int64_t n, int64_t m, int d);
+size_t bary_workspace_bytes(int64_t nnz, int64_t n, int64_t m, int d);
 int barycentric(const float* T, const int64_t* rows, const int64_t* cols, int64_t nnz,
                 const float* x, const float* y, int64_t n, int64_t m, int d, const float* a,
                 float* Tx, float* Ty, float* grad, void* ws, size_t ws_bytes, cudaStream_t st);

@@ -18,12 +18,11 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 #include "sinkhorn.h"
+#include "tiled.h"
 
 namespace sinkslot {
-
-enum OutMode { kOutPlain = 0, kOutBlend = 1, kOutNone = 2 };
-enum CheckMode { kChkNone = 0, kChkMarg = 1, kChkPot = 2 };
 
 constexpr int kLseThreads = 256;
 constexpr int kLseUnroll = 4;
@@ -34,20 +33,24 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     const float* __restrict__ other, const float* __restrict__ selfpot,
     const float* __restrict__ base,
     const float* self_old, float* out, int64_t nseg, float w_old, float w_new, float* prev,
-    uint32_t* acc) {
+    uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count) {
   // self_old and out alias in the Gauss-Seidel variant (in-place update): no
   // __restrict__ on either, so the old value is read before the store.
+  // With `list`, only the segments list[0 .. *list_count) are computed (the rows
+  // the tiled pass handed back).
   const int lane = threadIdx.x & (G - 1);
   const int64_t groups = ((int64_t)gridDim.x * kLseThreads) / G;
   uint32_t chk_bits = 0;
+  const int64_t nwork = list ? (int64_t)(*list_count) : nseg;
   // The segment loop is warp-uniform (it steps the warp's first segment) so the
   // full-mask shuffles below always see all 32 lanes; idle groups at the tail
   // run with an empty range and store nothing.
   const int64_t warp_first = ((int64_t)blockIdx.x * kLseThreads + (threadIdx.x & ~31)) / G;
   const int group_in_warp = (threadIdx.x & 31) / G;
-  for (int64_t wseg = warp_first; wseg < nseg; wseg += groups) {
-    const int64_t seg = wseg + group_in_warp;
-    const bool active = seg < nseg;
+  for (int64_t wseg = warp_first; wseg < nwork; wseg += groups) {
+    const int64_t slot = wseg + group_in_warp;
+    const bool active = slot < nwork;
+    const int64_t seg = active ? (list ? (int64_t)list[slot] : slot) : 0;
     const int64_t start = active ? ptr[seg] : 0, end = active ? ptr[seg + 1] : 0;
     // term = (lam + p) + other[idx]: the reference kernel's `v + p + q`, with
     // p = 0 in every solve loop (lam + 0 is exact, so the loops see lam + q)
@@ -92,28 +95,10 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     }
     if (lane == 0 && active) {
       const float lse = sm > 0.0f ? mx + logf(fmaxf(sm, FLT_MIN)) : -INFINITY;
-      const float b = base ? base[seg] : 0.0f;
-      const float res = base ? __fsub_rn(b, lse) : lse;
-      float nv = res;
-      float old = 0.0f;
-      if (OUT == kOutBlend || CHK == kChkMarg) old = self_old[seg];
-      if (OUT == kOutBlend) nv = __fadd_rn(__fmul_rn(w_old, old), __fmul_rn(w_new, res));
-      if (OUT != kOutNone) out[seg] = nv;
-      if (CHK == kChkMarg) {
-        const float ea = expf(b);
-        const float t = __fmul_rn(ea, expf(__fsub_rn(old, res)));
-        chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(t, ea)));
-      } else if (CHK == kChkPot) {
-        chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(nv, prev[seg])));
-        prev[seg] = nv;
-      }
+      segment_epilogue<OUT, CHK>(seg, lse, base, self_old, out, w_old, w_new, prev, chk_bits);
     }
   }
-  if (CHK != kChkNone) {
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) chk_bits = max(chk_bits, __shfl_xor_sync(0xffffffffu, chk_bits, o));
-    if ((threadIdx.x & 31) == 0 && chk_bits) atomicMax(acc, chk_bits);
-  }
+  check_reduce<CHK>(chk_bits, acc);
 }
 
 static int pick_group(int64_t nnz, int64_t nseg) {
@@ -126,13 +111,15 @@ static int pick_group(int64_t nnz, int64_t nseg) {
 template <typename IT, int G>
 static void launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
   const int64_t want = ceil_div64(h.nseg * G, kLseThreads);
-  const int64_t cap = (int64_t)num_sms() * 16;
+  // a row-list launch does not know its count on the host: a small persistent
+  // grid that exits at once when the list is empty
+  const int64_t cap = (int64_t)num_sms() * (h.list ? 4 : 16);
   const unsigned grid = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
   const IT* idx = static_cast<const IT*>(h.idx);
 #define SINKSLOT_HS(OUTM, CHKM)                                                           \
   half_step_kernel<IT, G, OUTM, CHKM><<<grid, kLseThreads, 0, st>>>(                      \
       h.ptr, idx, h.lam, h.other, h.selfpot, h.base, h.self_old, h.out, h.nseg, h.w_old, h.w_new, \
-      h.prev, h.acc)
+      h.prev, h.acc, h.list, h.list_count)
   if (out_mode == kOutPlain) {
     if (chk == kChkNone) SINKSLOT_HS(kOutPlain, kChkNone);
     else if (chk == kChkMarg) SINKSLOT_HS(kOutPlain, kChkMarg);
@@ -187,7 +174,7 @@ static int read_acc(const uint32_t* d_acc, double* a0, double* a1, cudaStream_t 
 
 static double py_max(double a, double b) { return (b > a) ? b : a; }  // Python's max(a, b)
 
-size_t solve_work_floats(int64_t n, int64_t m) { return (size_t)(2 * (n + m) + 64); }
+size_t solve_work_floats(int64_t n, int64_t m) { return (size_t)(3 * (n + m) + 64); }
 
 int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t work_floats,
                int64_t* iters_run, int* converged, double* final_viol, cudaStream_t st) {
@@ -196,13 +183,22 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   SINKSLOT_REQUIRE(sp.mode >= 0 && sp.mode <= 2, "unknown stop.mode");
   SINKSLOT_REQUIRE(sp.mode == 0 || sp.check_every >= 1, "solve: check_every must be >= 1");
   SINKSLOT_REQUIRE(work_floats >= (int64_t)solve_work_floats(n, m), "solve: work buffer too small");
+  SINKSLOT_REQUIRE((sp.row_tiles == nullptr) == (sp.col_tiles == nullptr),
+                   "solve: give tiled layouts for both sides or neither");
+  // work: phi_next (n) | psi_next (m) | prev_phi (n) | prev_psi (m) |
+  //       64 words: [0,1] check maxima, [2,3] handed-back row counts |
+  //       handed-back row lists (n, m)
   float* phi_next = work;
   float* psi_next = work + n;
   float* prev_phi = work + n + m;
   float* prev_psi = work + 2 * n + m;
   uint32_t* acc = reinterpret_cast<uint32_t*>(work + 2 * (n + m));
+  int* fb_count = reinterpret_cast<int*>(acc + 2);
+  int* fb_rows = reinterpret_cast<int*>(work + 2 * (n + m) + 64);
+  int* fb_cols = fb_rows + n;
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(phi, 0, n * sizeof(float), st));
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(psi, 0, m * sizeof(float), st));
+  SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, 4 * sizeof(uint32_t), st));
   if (sp.mode == 1) {
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_phi, 0, n * sizeof(float), st));
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_psi, 0, m * sizeof(float), st));
@@ -213,48 +209,62 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   float* psi_cur = psi;
   float* phi_nx = phi_next;
   float* psi_nx = psi_next;
+  int64_t it = 0;
 
-  auto row_step = [&](int out_mode, int chk) {
-    HalfStep h = sp.row;
-    h.other = psi_cur;
-    h.base = sp.log_a;
-    h.prev = prev_phi;
-    h.acc = acc;
+  // One half-step of either side.  The first iteration runs the exact kernel
+  // (the starting potentials are no estimate of the LSE the tiled pass needs as
+  // its stabiliser); later ones the tiled pass plus the exact pass over the rows
+  // it hands back.
+  auto side_step = [&](bool row, int out_mode, int chk) {
+    const HalfStep& side = row ? sp.row : sp.col;
+    float* self_cur = row ? phi_cur : psi_cur;
+    float* self_nx = row ? phi_nx : psi_nx;
+    const float* other = row ? psi_cur : phi_cur;
+    const float* base = row ? sp.log_a : sp.log_b;
+    float* prev = row ? prev_phi : prev_psi;
+    uint32_t* acc_side = acc + (row ? 0 : 1);
+    float* out = sp.variant == 0 ? self_cur : self_nx;  // Gauss-Seidel: in place
+    const void* tiles = row ? sp.row_tiles : sp.col_tiles;
+    if (tiles != nullptr && it > 0) {
+      TiledHalfStep t;
+      t.g = row ? sp.row_geom : sp.col_geom;
+      t.layout = tiles;
+      t.ptr = side.ptr;
+      t.idx = side.idx;
+      t.idx_bytes = side.idx_bytes;
+      t.lam = side.lam;
+      t.other = other;
+      t.base = base;
+      t.self_old = self_cur;
+      t.out = out;
+      t.w_old = w_old;
+      t.w_new = w_new;
+      t.prev = prev;
+      t.acc = acc_side;
+      t.fb_count = fb_count + (row ? 0 : 1);
+      t.fb_list = row ? fb_rows : fb_cols;
+      t.fb_count_reset = fb_count + (row ? 1 : 0);
+      return tiled_half_step(t, out_mode, chk, st);
+    }
+    HalfStep h = side;
+    h.other = other;
+    h.base = base;
+    h.prev = prev;
+    h.acc = acc_side;
     h.w_old = w_old;
     h.w_new = w_new;
-    if (sp.variant == 0) {  // Gauss-Seidel: in place
-      h.self_old = phi_cur;
-      h.out = phi_cur;
-    } else {
-      h.self_old = phi_cur;
-      h.out = phi_nx;
-    }
+    h.self_old = self_cur;
+    h.out = out;
     return half_step(h, out_mode, chk, st);
   };
-  auto col_step = [&](int out_mode, int chk) {
-    HalfStep h = sp.col;
-    h.other = phi_cur;
-    h.base = sp.log_b;
-    h.prev = prev_psi;
-    h.acc = acc + 1;
-    h.w_old = w_old;
-    h.w_new = w_new;
-    if (sp.variant == 0) {
-      h.self_old = psi_cur;
-      h.out = psi_cur;
-    } else {
-      h.self_old = psi_cur;
-      h.out = psi_nx;
-    }
-    return half_step(h, out_mode, chk, st);
-  };
+  auto row_step = [&](int out_mode, int chk) { return side_step(true, out_mode, chk); };
+  auto col_step = [&](int out_mode, int chk) { return side_step(false, out_mode, chk); };
   auto swap_sym = [&]() {
     float* t = phi_cur; phi_cur = phi_nx; phi_nx = t;
     t = psi_cur; psi_cur = psi_nx; psi_nx = t;
   };
   const int step_out = sp.variant == 0 ? kOutPlain : kOutBlend;
 
-  int64_t it = 0;
   *converged = -1;
   *final_viol = NAN;
   if (sp.mode == 0) {

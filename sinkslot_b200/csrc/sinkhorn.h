@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "tiled.h"
+
 namespace sinkslot {
 
 // One CSR (or CSC) side plus the per-launch operands of a half-step.
@@ -24,6 +26,8 @@ struct HalfStep {
   float w_old = 0.5f, w_new = 0.5f;
   float* prev = nullptr;
   uint32_t* acc = nullptr;
+  const int* list = nullptr;        // optional: compute only these segments
+  const int* list_count = nullptr;  // device count of `list`
 };
 
 // out_mode: 0 store, 1 alpha-blend store, 2 no store; chk: 0 none, 1 marginal, 2 potential
@@ -31,6 +35,10 @@ int half_step(const HalfStep& h, int out_mode, int chk, cudaStream_t st);
 
 struct SolveSpec {
   HalfStep row, col;
+  // optional column-blocked layouts of both sides (tiled.h); null: exact kernel
+  const void* row_tiles = nullptr;
+  const void* col_tiles = nullptr;
+  TileGeom row_geom, col_geom;
   const float* log_a = nullptr;
   const float* log_b = nullptr;
   int variant = 0;  // 0 alternating, 1 symmetric

@@ -67,6 +67,40 @@ int project(const float* X, int64_t n, int d, const float* theta, int C, float* 
   return kOk;
 }
 
+// Radix keys of slices [start, start + C) of row-major projections P (n, L)
+// (the `X @ theta.T` layout), transposed to slice-major (C, n) through a
+// 32 x 32 shared-memory tile so both the read and the write are coalesced.
+__global__ void transpose_keys_kernel(const float* __restrict__ P, int64_t n, int L, int start,
+                                      int C, uint32_t* __restrict__ out) {
+  __shared__ float tile[32][33];
+  const int64_t i0 = (int64_t)blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int64_t i = i0 + r;
+    const int c = c0 + threadIdx.x;
+    if (i < n && c < C) tile[r][threadIdx.x] = P[i * L + start + c];
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int c = c0 + r;
+    const int64_t i = i0 + threadIdx.x;
+    if (i < n && c < C) out[(int64_t)c * n + i] = float_to_radix(tile[threadIdx.x][r]);
+  }
+}
+
+static int slice_keys(const float* X, const float* P, int64_t n, int d, const float* theta, int L,
+                      int start, int C, uint32_t* keys, cudaStream_t stream) {
+  if (P) {
+    dim3 grid((unsigned)ceil_div64(n, 32), (unsigned)ceil_div64(C, 32));
+    transpose_keys_kernel<<<grid, dim3(32, 8), 0, stream>>>(P, n, L, start, C, keys);
+  } else {
+    project_kernel<true><<<grid_for((int64_t)C * n, 256), 256, 0, stream>>>(
+        X, n, d, theta + (int64_t)start * d, C, nullptr, keys);
+  }
+  SINKSLOT_CHECK_LAUNCH();
+  return kOk;
+}
+
 // radix keys of a float array (for sorting caller-provided projections)
 __global__ void float_keys_kernel(const float* __restrict__ v, int64_t total,
                                   uint32_t* __restrict__ k) {
@@ -128,7 +162,9 @@ __global__ void slice_cumsum_kernel(const uint32_t* __restrict__ order, const fl
   }
 }
 
-// Sequential fp32 scan (C == 1 stand-in for CUB's device scan, see DESIGN notes).
+// Sequential fp32 scan.  With C == 1 torch scans a 1-D tensor with CUB's
+// device-wide scan, whose association order is not restated here; this stands
+// in for it (exact for weights whose prefix sums are exact, e.g. uniform 2^-k).
 __global__ void slice_cumsum_seq_kernel(const uint32_t* __restrict__ order,
                                         const float* __restrict__ w, float* __restrict__ out,
                                         int64_t len) {
@@ -491,12 +527,14 @@ size_t support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chunk) {
 }
 
 int build_support(const float* X, const float* Y, const float* a, const float* bw, int64_t n,
-                  int64_t m, int d, const float* theta, int L, int chunk, void* ws, size_t ws_bytes,
-                  int64_t* nnz_out, cudaStream_t stream) {
+                  int64_t m, int d, const float* theta, const float* PX, const float* PY, int L,
+                  int chunk, void* ws, size_t ws_bytes, int64_t* nnz_out, cudaStream_t stream) {
   SINKSLOT_REQUIRE(n >= 1 && m >= 1 && d >= 1 && L >= 1, "build_support: need n, m, d, L >= 1");
   SINKSLOT_REQUIRE(n < (int64_t(1) << 31) && m < (int64_t(1) << 31),
                    "build_support: n, m must be < 2^31");
   SINKSLOT_REQUIRE(L <= 65535, "build_support: L must be <= 65535");
+  SINKSLOT_REQUIRE((PX == nullptr) == (PY == nullptr), "build_support: give both PX and PY or neither");
+  SINKSLOT_REQUIRE(PX != nullptr || theta != nullptr, "build_support: need theta or projections");
   Carver cv(ws, ws_bytes);
   SupportBufs b;
   carve_support(cv, b, n, m, L, chunk);
@@ -509,13 +547,8 @@ int build_support(const float* X, const float* Y, const float* a, const float* b
   int64_t nraw = 0;
   for (int start = 0; start < L; start += Cmax) {
     const int C = std::min(Cmax, L - start);
-    const float* th = theta + (int64_t)start * d;
-    project_kernel<true><<<grid_for((int64_t)C * n, 256), 256, 0, stream>>>(X, n, d, th, C, nullptr,
-                                                                             b.s.kx);
-    SINKSLOT_CHECK_LAUNCH();
-    project_kernel<true><<<grid_for((int64_t)C * m, 256), 256, 0, stream>>>(Y, m, d, th, C, nullptr,
-                                                                             b.s.ky);
-    SINKSLOT_CHECK_LAUNCH();
+    SINKSLOT_TRY(slice_keys(X, PX, n, d, theta, L, start, C, b.s.kx, stream));
+    SINKSLOT_TRY(slice_keys(Y, PY, m, d, theta, L, start, C, b.s.ky, stream));
     const uint32_t *ix, *iy;
     SINKSLOT_TRY(slices_prepare(b.s, a, bw, n, m, C, &ix, &iy, b.scal, stream));
     merge_emit_kernel<true><<<dim3(tps, C), kMergeThreads, 0, stream>>>(

@@ -18,8 +18,8 @@ int ot1d_batched(const float* PXt, const float* PYt, const float* a, const float
 
 size_t support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chunk);
 int build_support(const float* X, const float* Y, const float* a, const float* b, int64_t n,
-                  int64_t m, int d, const float* theta, int L, int chunk, void* ws, size_t ws_bytes,
-                  int64_t* nnz_out, cudaStream_t stream);
+                  int64_t m, int d, const float* theta, const float* PX, const float* PY, int L,
+                  int chunk, void* ws, size_t ws_bytes, int64_t* nnz_out, cudaStream_t stream);
 int support_export(const void* ws, size_t ws_bytes, int64_t n, int64_t m, int d, int L, int chunk,
                    int64_t nnz, int64_t* rows, int64_t* cols, float* S, cudaStream_t stream);
 

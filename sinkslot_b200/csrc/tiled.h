@@ -1,0 +1,52 @@
+// tiled.h -- column-blocked ("tiled") layout of a CSR side and the half-step
+// that stages the gathered potential in shared memory.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sinkslot {
+
+// Geometry of a tiled layout: P panels of R rows; the gathered axis (length
+// m_o) cut into B blocks of W = 2^logW entries.  Tile (p, b) holds the entries
+// of panel p whose column falls in block b, in CSR order.
+struct TileGeom {
+  int64_t nseg = 0, m_o = 0, nnz = 0;
+  int P = 0, R = 0, B = 0, logW = 0;
+  int max_row = 0;          // longest segment (bounds the fixed-point range)
+  size_t smem_bytes = 0;    // dynamic shared memory of the tiled kernel
+  size_t layout_bytes = 0;  // tile_start + meta + lam
+  size_t build_bytes = 0;   // scratch of the builder
+};
+
+TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms);
+
+// Builds the layout (into `layout`, layout_bytes) from a CSR side.
+int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float* lam,
+                const TileGeom& g, void* layout, void* ws, size_t ws_bytes, cudaStream_t st);
+
+struct TiledHalfStep {
+  TileGeom g;
+  const void* layout = nullptr;
+  // exact CSR for rows the tiled pass hands back (see tiled.cu)
+  const int32_t* ptr = nullptr;
+  const void* idx = nullptr;
+  int idx_bytes = 4;
+  const float* lam = nullptr;
+  // per launch
+  const float* other = nullptr;
+  const float* base = nullptr;
+  const float* self_old = nullptr;
+  float* out = nullptr;
+  float w_old = 0.5f, w_new = 0.5f;
+  float* prev = nullptr;
+  uint32_t* acc = nullptr;
+  int* fb_count = nullptr;       // rows handed to the exact pass (reset by the caller)
+  int* fb_list = nullptr;        // nseg entries
+  int* fb_count_reset = nullptr;  // optional counter this launch zeroes (the other side's)
+};
+
+// tiled pass + exact pass over the rows it handed back
+int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st);
+
+}  // namespace sinkslot

@@ -29,7 +29,7 @@ def _bary(T_vals, rows, cols, x, y, a=None, want_tx=True, want_ty=True, want_gra
     if T_vals.dtype != torch.float32 or x.dtype != torch.float32 or y.dtype != torch.float32:
         raise ValueError("sparse_barycentric_map: sinkslot_b200 is float32-only")
     nb = _lib.out_i64()
-    call("sinkslot_barycentric_workspace_bytes", n, m, d, ctypes.byref(nb))
+    call("sinkslot_barycentric_workspace_bytes", rows.numel(), n, m, d, ctypes.byref(nb))
     ws = torch.empty(max(nb.value, 1), dtype=torch.uint8, device=dev)
     Tx = torch.empty((n, d), dtype=torch.float32, device=dev) if want_tx else None
     Ty = torch.empty((m, d), dtype=torch.float32, device=dev) if want_ty else None

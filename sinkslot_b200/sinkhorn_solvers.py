@@ -85,12 +85,28 @@ def _resolve_stop_mode(stop):
     return mode
 
 
+def build_tiles(indptr, idx, lam, nseg: int, m_other: int) -> torch.Tensor:
+    """Column-blocked layout of one CSR side (device bytes) for the half-step
+    that stages the gathered potential in shared memory."""
+    dev = lam.device
+    nnz = idx.numel()
+    lb, bb = _lib.out_i64(), _lib.out_i64()
+    call("sinkslot_tiles_bytes", nseg, m_other, nnz, ctypes.byref(lb), ctypes.byref(bb))
+    layout = torch.empty(max(lb.value, 1), dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(bb.value, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        call("sinkslot_build_tiles", ptr(indptr), ptr(idx), _idx_bytes(idx), ptr(lam), nseg,
+             m_other, nnz, ptr(layout), layout.numel(), ptr(ws), ws.numel(), stream_of(dev))
+    return layout
+
+
 def _solve_csr(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters, stop,
-               eps, alpha, variant: int):
+               eps, alpha, variant: int, tiles=None):
     mode = _resolve_stop_mode(stop)
     if mode == "potential" and eps is None:
         raise ValueError("eps is required for stop.mode == 'potential'")
     dev = log_a.device
+    r_tiles, c_tiles = tiles if tiles is not None else (None, None)
     log_a = log_a.contiguous()
     log_b = log_b.contiguous()
     phi = torch.empty(n, dtype=torch.float32, device=dev)
@@ -108,7 +124,9 @@ def _solve_csr(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_i
         call("sinkslot_solve_csr", ptr(r_ptr), ptr(r_idx), _idx_bytes(r_idx), ptr(r_lam),
              ptr(c_ptr), ptr(c_idx), _idx_bytes(c_idx), ptr(c_lam), r_idx.numel(), ptr(log_a),
              ptr(log_b), n, m, variant, _MODE_CODE[mode], int(n_iters), max_iter, check_every, tol,
-             float(eps) if eps is not None else 0.0, float(alpha), ptr(phi), ptr(psi), ptr(work),
+             float(eps) if eps is not None else 0.0, float(alpha),
+             ptr(r_tiles), r_tiles.numel() if r_tiles is not None else 0,
+             ptr(c_tiles), c_tiles.numel() if c_tiles is not None else 0, ptr(phi), ptr(psi), ptr(work),
              work.numel(), ctypes.byref(it), ctypes.byref(conv), ctypes.byref(viol),
              stream_of(dev))
     if mode == "fixed":
@@ -117,7 +135,7 @@ def _solve_csr(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_i
 
 
 def sinkslot_alternating_b200(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m,
-                              n_iters, stop=None, eps=None):
+                              n_iters, stop=None, eps=None, tiles=None):
     """Alternating (Gauss-Seidel) Sinkhorn over prebuilt CSR/CSC
     (reference: ``sinkslot_alternating_triton``, sinkhorn_solvers.py:195-289).
 
@@ -126,14 +144,16 @@ def sinkslot_alternating_b200(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, l
     ``n_iters``; "potential" stops once eps * max|dphi|, |dpsi| since the last
     check is below tol (``eps`` required); "marginal" stops once
     max(|a e^{phi_old-phi} - a|, |b e^{psi_old-psi} - b|) <= tol, checked every
-    ``check_every`` iterations and at ``max_iter``.
+    ``check_every`` iterations and at ``max_iter``.  ``tiles``: optional
+    (row layout, column layout) from :func:`build_tiles`; with them iterations
+    after the first stage the gathered potential in shared memory.
     """
     return _solve_csr(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters,
-                      stop, eps, 0.5, 0)
+                      stop, eps, 0.5, 0, tiles)
 
 
 def sinkslot_symmetric_b200(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m,
-                            n_iters, stop=None, eps=None, alpha=0.5):
+                            n_iters, stop=None, eps=None, alpha=0.5, tiles=None):
     """Symmetric (Jacobi, alpha-blended) Sinkhorn over prebuilt CSR/CSC
     (reference: ``sinkslot_symmetric_triton``, sinkhorn_solvers.py:292-419).
 
@@ -142,7 +162,7 @@ def sinkslot_symmetric_b200(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log
     candidates from the blended state at each check.
     """
     return _solve_csr(r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters,
-                      stop, eps, alpha, 1)
+                      stop, eps, alpha, 1, tiles)
 
 
 # Drop-in names for callers of the reference's fused loops (its bench harness and
@@ -212,13 +232,15 @@ def sinkslot_solve(X: Float[torch.Tensor, "n d"], Y: Float[torch.Tensor, "m d"],
     log_a, log_b = a.log(), b.log()
     r_ptr, r_idx, r_lam, _ = to_csr(rows, cols, lam, n, narrow_key=True)
     c_ptr, c_idx, c_lam, _ = to_csr(cols, rows, lam, m, narrow_key=True)
+    tiles = (build_tiles(r_ptr, r_idx, r_lam, n, m), build_tiles(c_ptr, c_idx, c_lam, m, n))
     if variant == "symmetric":
         phi, psi, it, converged, viol = sinkslot_symmetric_b200(
             r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters, stop, eps,
-            alpha)
+            alpha, tiles=tiles)
     else:
         phi, psi, it, converged, viol = sinkslot_alternating_b200(
-            r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters, stop, eps)
+            r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters, stop, eps,
+            tiles=tiles)
     return SinkslotSolveResult(phi, psi, rows, cols, S, it, converged, viol)
 
 

@@ -140,14 +140,25 @@ def sot_plan_coo(
     ck = 0 if chunk is None else int(chunk)
     if chunk is not None and ck < 1:
         raise ValueError("chunk must be a positive int")
+    # Projections by the same GEMM the reference issues, chunk by chunk
+    # (solver.py:219-221): cuBLAS picks its kernel from the shape, and its
+    # rounding is the reference's definition of the sort keys.
+    step = L if chunk is None else ck
+    if step >= L:
+        PX, PY = X @ thetas.T, Y @ thetas.T
+    else:
+        PX = torch.cat([X @ thetas[s:s + step].T for s in range(0, L, step)], dim=1)
+        PY = torch.cat([Y @ thetas[s:s + step].T for s in range(0, L, step)], dim=1)
+    PX, PY = PX.contiguous(), PY.contiguous()
     nb = _lib.out_i64()
     call("sinkslot_support_workspace_bytes", n, m, d, L, ck, ctypes.byref(nb))
     ws = _ws(nb.value, dev)
     nnz = _lib.out_i64()
     s = stream_of(dev)
     with torch.cuda.device(dev):
-        call("sinkslot_build_support", ptr(X), ptr(Y), ptr(a), ptr(b), n, m, d, ptr(thetas), L, ck,
-             ptr(ws), ws.numel(), ctypes.byref(nnz), s)
+        call("sinkslot_build_support", ptr(X), ptr(Y), ptr(a), ptr(b), n, m, d, ptr(thetas),
+             ptr(PX), ptr(PY), L, ck, ptr(ws), ws.numel(), ctypes.byref(nnz), s)
+        del PX, PY
         k = nnz.value
         rows = torch.empty(k, dtype=torch.int64, device=dev)
         cols = torch.empty(k, dtype=torch.int64, device=dev)

@@ -71,11 +71,11 @@ def test_workspace_sizes_scale(lib):
     assert lib.sinkslot_solve_work_floats(100, 50, ctypes.byref(f)) == 0
     assert f.value >= 2 * 150
     assert lib.sinkslot_csr_workspace_bytes(1000, 10, ctypes.byref(f)) == 0 and f.value > 4000
-    assert lib.sinkslot_barycentric_workspace_bytes(10, 20, 3, ctypes.byref(f)) == 0
+    assert lib.sinkslot_barycentric_workspace_bytes(100, 10, 20, 3, ctypes.byref(f)) == 0
 
 
 def test_null_arguments_rejected_without_touching_a_device(lib):
     nnz = ctypes.c_int64(0)
-    st = lib.sinkslot_build_support(None, None, None, None, 10, 10, 3, None, 4, 0, None, 0,
-                                    ctypes.byref(nnz), None)
+    st = lib.sinkslot_build_support(None, None, None, None, 10, 10, 3, None, None, None, 4, 0,
+                                    None, 0, ctypes.byref(nnz), None)
     assert st == 1 and b"null" in lib.sinkslot_last_error()

@@ -84,12 +84,24 @@ def test_fixed_solve_matches_oracle(cuda, oracle, case, variant):
     np.testing.assert_array_equal(res.rows.cpu().numpy(), o.rows)
     assert_close_np(res.phi.cpu().numpy(), o.phi, RTOL, ATOL, "phi")
     assert_close_np(res.psi.cpu().numpy(), o.psi, RTOL, ATOL, "psi")
-    # against the reference's own CPU run when its support is the same
+    # Against the reference's own CPU run: strict where its support and S are
+    # this device's (the CPU run accumulates cumsums in double, so S can differ
+    # in the last bit); otherwise after removing the (+c, -c) shift, which the
+    # iteration leaves undamped and so carries any difference in S.
     key = "alt" if variant == "alternating" else "sym"
-    if "rows_cudabuilder" in g and np.array_equal(o.rows, g["rows_cudabuilder"]) and \
-            np.array_equal(o.cols, g["cols_cudabuilder"]):
-        assert_close_np(res.phi.cpu().numpy(), g[f"phi_{key}"], RTOL, ATOL, "phi vs reference")
-        assert_close_np(res.psi.cpu().numpy(), g[f"psi_{key}"], RTOL, ATOL, "psi vs reference")
+    if "rows_cudabuilder" not in g:
+        return
+    same = (np.array_equal(o.rows, g["rows_cudabuilder"]) and
+            np.array_equal(o.cols, g["cols_cudabuilder"]) and np.array_equal(o.S, g["S_cudabuilder"]))
+    phi, psi = res.phi.cpu().numpy(), res.psi.cpu().numpy()
+    if same:
+        assert_close_np(phi, g[f"phi_{key}"], RTOL, ATOL, "phi vs reference")
+        assert_close_np(psi, g[f"psi_{key}"], RTOL, ATOL, "psi vs reference")
+    else:
+        fin = np.isfinite(g[f"phi_{key}"])
+        c = float(np.mean(phi[fin].astype(np.float64) - g[f"phi_{key}"][fin]))
+        assert_close_np(phi - np.float32(c), g[f"phi_{key}"], RTOL, 1e-4, "centred phi vs reference")
+        assert_close_np(psi + np.float32(c), g[f"psi_{key}"], RTOL, 1e-4, "centred psi vs reference")
 
 
 @pytest.mark.parametrize("variant", ["alternating", "symmetric"])
@@ -144,12 +156,19 @@ def test_full_size_alternating_matches_torch_reference_ops(cuda):
     res = sinkslot_solve(X, Y, a, a, 0.01, 64, 0, 500)
     lam, _ = cost_and_lam(X, Y, res.rows, res.cols, res.S, 0.01)
     phi, psi = alternating_fixed(res.rows, res.cols, lam, a.log(), a.log(), n, n, 500)
-    d_phi = (res.phi - phi).abs()
-    bad = d_phi > ATOL + RTOL * phi.abs()
-    assert int(bad.sum()) == 0, f"{int(bad.sum())} phi outside tol, max {float(d_phi.max()):.3e}"
-    d_psi = (res.psi - psi).abs()
-    bad = d_psi > ATOL + RTOL * psi.abs()
-    assert int(bad.sum()) == 0, f"{int(bad.sum())} psi outside tol, max {float(d_psi.max()):.3e}"
+    # Raw per-element agreement: the rtol/atol bar holds except for potentials
+    # within ~1e-3 of zero, where the difference is the common (+c, -c) shift
+    # that 500 iterations accumulate from last-bit differences in exp/log; the
+    # reference's own backends differ from each other the same way.
+    d_phi = (res.phi - phi).double()
+    d_psi = (res.psi - psi).double()
+    bad = (d_phi.abs() > ATOL + RTOL * phi.abs()).sum() + (d_psi.abs() > ATOL + RTOL * psi.abs()).sum()
+    assert int(bad) <= 2e-4 * (2 * n), f"{int(bad)} potentials outside rtol/atol"
+    c = float(d_phi.mean())
+    assert abs(c) < 1e-3 and abs(float(d_psi.mean()) + c) < 1e-4
+    # after removing the shift, every element is within the bar
+    torch.testing.assert_close(res.phi - c, phi, rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(res.psi + c, psi, rtol=RTOL, atol=ATOL)
     # column marginal is exact after the column half-step (size-independent property)
     P = (res.phi[res.rows] + res.psi[res.cols] + lam).exp()
     col = torch.zeros(n, device=cuda, dtype=torch.float64).index_add_(0, res.cols, P.double())
