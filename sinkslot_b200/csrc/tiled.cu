@@ -15,12 +15,15 @@
 // Arithmetic: the log-sum-exp of a row is stabilised by the row's previous
 // value, sigma = base - self_old (the LSE the previous half-step produced), so
 // each term exp(lam + other - sigma) is O(1) and the terms of a row can be
-// added in any order: they are accumulated as 64-bit fixed point (2^-40 units)
-// with shared-memory integer atomics, which makes the sum exact and
-// order-independent (deterministic).  A row is handed back to the exact
-// (max-stabilised) kernel when a term would leave the fixed-point range or its
-// sum is below 2^-8 -- the first iteration, where sigma is not yet an estimate,
-// and any row whose potential moved by more than a few units.
+// added in any order: each term is rounded to fixed point in 2^-32 units,
+// split into a high part (bits 20+) and a low part (bits 0-19), and the parts
+// are summed with native 32-bit shared-memory integer atomics -- exact and
+// order-independent, so the result is deterministic.  The high-part sum cannot
+// overflow because terms are capped at 2^k with k = 20 - ceil(log2(longest
+// row)); the low-part sum cannot overflow for rows of up to 4096 entries.  A
+// row is handed back to the exact (max-stabilised) kernel when a term exceeds
+// the cap or its sum is below 2^-8 -- the first iteration, where sigma is not
+// yet an estimate, and any row whose potential moved by more than a few units.
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -36,13 +39,14 @@ namespace sinkslot {
 constexpr int kTileThreads = 1024;
 constexpr int kTileUnroll = 8;
 constexpr size_t kSmemCap = 227 * 1024;
-constexpr float kFixScale = 1099511627776.0f;  // 2^40
-constexpr double kFixInv = 1.0 / 1099511627776.0;
-constexpr unsigned long long kFixMin = 1ull << 32;  // sums below 2^-8 go to the exact pass
+constexpr float kFixScale = 4294967296.0f;  // 2^32
+constexpr double kFixInv = 1.0 / 4294967296.0;
+constexpr unsigned long long kFixMin = 1ull << 24;  // sums below 2^-8 go to the exact pass
+constexpr int kLoBits = 20;
 
+// shared memory per panel row: sigma, high sum, low sum (4 B each) + a flag bit
 static size_t rows_smem(int R) {
-  return align_up((size_t)R * 8, 16) + align_up((size_t)R * 4, 16) +
-         align_up((size_t)((R + 31) / 32) * 4, 16);
+  return 3 * align_up((size_t)R * 4, 16) + align_up((size_t)((R + 31) / 32) * 4, 16);
 }
 
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
@@ -282,34 +286,54 @@ template <int OUT, int CHK>
 __global__ void __launch_bounds__(kTileThreads, 1) tiled_half_step_kernel(const TKArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int W = 1 << a.logW;
+  const size_t rbytes = align_up((size_t)a.R * 4, 16);
   float* pot0 = reinterpret_cast<float*>(smem);
   float* pot1 = pot0 + W;
-  unsigned long long* accs = reinterpret_cast<unsigned long long*>(smem + (size_t)2 * 4 * W);
-  float* sig = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(accs) +
-                                        align_up((size_t)a.R * 8, 16));
-  uint32_t* flags = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(sig) +
-                                                align_up((size_t)a.R * 4, 16));
+  float* sig = reinterpret_cast<float*>(smem + (size_t)2 * 4 * W);
+  uint32_t* hi = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(sig) + rbytes);
+  uint32_t* lo = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(hi) + rbytes);
+  uint32_t* flags = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(lo) + rbytes);
   if (a.fb_reset && blockIdx.x == 0 && threadIdx.x == 0) *a.fb_reset = 0;
 
-  // terms above capd would overflow the 64-bit fixed-point sum of the longest row
+  // Terms are capped at 2^k, k = 20 - ceil(log2(longest row)), so the high-part
+  // sum of any row stays below 2^32; longer rows than 4096 would overflow the
+  // low-part sum, and then every row goes to the exact pass.
   const long long longest = a.header[0] > 0 ? a.header[0] : 1;
-  const float capd = logf(4611686018427387904.0f / kFixScale / (float)longest);  // 2^62
+  int lg = 0;
+  while ((1ll << lg) < longest) ++lg;
+  const int k = kLoBits - lg;
+  const float capd = (longest <= 4096 && k >= 1) ? ((float)k - 0.01f) * 0.69314718f : -INFINITY;
   uint32_t chk_bits = 0;
+  constexpr int64_t kRound = (int64_t)kTileThreads * kTileUnroll;
 
   for (int p = blockIdx.x; p < a.P; p += gridDim.x) {
     const int64_t row0 = (int64_t)p * a.R;
     const int rows = (int)std::min<int64_t>(a.R, a.nseg - row0);
     if (rows <= 0) break;
+    const int64_t pb = (int64_t)p * a.B;
     for (int r = threadIdx.x; r < a.R; r += kTileThreads) {
-      accs[r] = 0ull;
+      hi[r] = 0u;
+      lo[r] = 0u;
       sig[r] = r < rows ? __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]) : 0.0f;
     }
     for (int r = threadIdx.x; r < (a.R + 31) / 32; r += kTileThreads) flags[r] = 0u;
     stage_block(a, 0, pot0);
     cp_async_commit();
+    // entries of the first round of tile 0, loaded while the block stages
+    uint32_t mt[kTileUnroll];
+    float lv[kTileUnroll];
+    {
+      const int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
+#pragma unroll
+      for (int u = 0; u < kTileUnroll; ++u) {
+        const int64_t e = e0 + (int64_t)u * kTileThreads + threadIdx.x;
+        mt[u] = e < e1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
+        lv[u] = e < e1 ? ld_stream(a.lam + e) : 0.0f;
+      }
+    }
     __syncthreads();
     for (int b = 0; b < a.B; ++b) {
-      float* cur = (b & 1) ? pot1 : pot0;
+      const float* cur = (b & 1) ? pot1 : pot0;
       if (b + 1 < a.B) {
         stage_block(a, b + 1, (b & 1) ? pot0 : pot1);
         cp_async_commit();
@@ -318,17 +342,22 @@ __global__ void __launch_bounds__(kTileThreads, 1) tiled_half_step_kernel(const 
         cp_async_wait<0>();
       }
       __syncthreads();
-      const int64_t e0 = a.tstart[(int64_t)p * a.B + b];
-      const int64_t e1 = a.tstart[(int64_t)p * a.B + b + 1];
-      for (int64_t base_e = e0; base_e < e1; base_e += (int64_t)kTileThreads * kTileUnroll) {
-        uint32_t mt[kTileUnroll];
-        float lv[kTileUnroll];
+      const int64_t e0 = a.tstart[pb + b];
+      const int64_t e1 = a.tstart[pb + b + 1];
+      // prefetch the next tile's first round; it lands while this tile computes
+      uint32_t nmt[kTileUnroll];
+      float nlv[kTileUnroll];
+      {
+        const int64_t f0 = e1;
+        const int64_t f1 = (b + 1 < a.B) ? a.tstart[pb + b + 2] : e1;
 #pragma unroll
         for (int u = 0; u < kTileUnroll; ++u) {
-          const int64_t e = base_e + (int64_t)u * kTileThreads + threadIdx.x;
-          mt[u] = e < e1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
-          lv[u] = e < e1 ? ld_stream(a.lam + e) : 0.0f;
+          const int64_t e = f0 + (int64_t)u * kTileThreads + threadIdx.x;
+          nmt[u] = e < f1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
+          nlv[u] = e < f1 ? ld_stream(a.lam + e) : 0.0f;
         }
+      }
+      for (int64_t base_e = e0;;) {
 #pragma unroll
         for (int u = 0; u < kTileUnroll; ++u) {
           if (mt[u] == 0xFFFFFFFFu) continue;
@@ -338,16 +367,31 @@ __global__ void __launch_bounds__(kTileThreads, 1) tiled_half_step_kernel(const 
           if (!(d <= capd)) {
             atomicOr(flags + (r >> 5), 1u << (r & 31));
           } else {
-            const float t = __expf(d);
-            atomicAdd(accs + r, __float2ull_rn(t * kFixScale));
+            const unsigned long long q = __float2ull_rn(__expf(d) * kFixScale);
+            atomicAdd(hi + r, (uint32_t)(q >> kLoBits));
+            atomicAdd(lo + r, (uint32_t)(q & ((1u << kLoBits) - 1u)));
           }
         }
+        base_e += kRound;
+        if (base_e >= e1) break;
+        // tiles longer than one round: the further rounds load in place
+#pragma unroll
+        for (int u = 0; u < kTileUnroll; ++u) {
+          const int64_t e = base_e + (int64_t)u * kTileThreads + threadIdx.x;
+          mt[u] = e < e1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
+          lv[u] = e < e1 ? ld_stream(a.lam + e) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kTileUnroll; ++u) {
+        mt[u] = nmt[u];
+        lv[u] = nlv[u];
       }
       __syncthreads();
     }
     for (int r = threadIdx.x; r < rows; r += kTileThreads) {
       const int64_t seg = row0 + r;
-      const unsigned long long q = accs[r];
+      const unsigned long long q = ((unsigned long long)hi[r] << kLoBits) + lo[r];
       const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
       if (flagged || q < kFixMin) {
         a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;

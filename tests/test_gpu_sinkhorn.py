@@ -84,24 +84,30 @@ def test_fixed_solve_matches_oracle(cuda, oracle, case, variant):
     np.testing.assert_array_equal(res.rows.cpu().numpy(), o.rows)
     assert_close_np(res.phi.cpu().numpy(), o.phi, RTOL, ATOL, "phi")
     assert_close_np(res.psi.cpu().numpy(), o.psi, RTOL, ATOL, "psi")
-    # Against the reference's own CPU run: strict where its support and S are
-    # this device's (the CPU run accumulates cumsums in double, so S can differ
-    # in the last bit); otherwise after removing the (+c, -c) shift, which the
-    # iteration leaves undamped and so carries any difference in S.
+    # Against the reference's own CPU run.  Its CPU cumsums accumulate in double
+    # while its CUDA run (this device) scans in fp32, so the two reference runs
+    # can cut the merged breakpoints differently: same support with different
+    # sliver masses, or a different support.  Strict where support and S are
+    # identical; otherwise the reference test's own criterion for its two
+    # builders ("different supports, same transport", test_sinkslot_bench.py:
+    # 111-129): the dense S plans agree to atol 1e-5.
     key = "alt" if variant == "alternating" else "sym"
     if "rows_cudabuilder" not in g:
         return
-    same = (np.array_equal(o.rows, g["rows_cudabuilder"]) and
-            np.array_equal(o.cols, g["cols_cudabuilder"]) and np.array_equal(o.S, g["S_cudabuilder"]))
-    phi, psi = res.phi.cpu().numpy(), res.psi.cpu().numpy()
+    gr, gc, gS = g["rows_cudabuilder"], g["cols_cudabuilder"], g["S_cudabuilder"]
+    same = (o.rows.size == gr.size and np.array_equal(o.rows, gr) and np.array_equal(o.cols, gc)
+            and np.array_equal(o.S, gS))
     if same:
-        assert_close_np(phi, g[f"phi_{key}"], RTOL, ATOL, "phi vs reference")
-        assert_close_np(psi, g[f"psi_{key}"], RTOL, ATOL, "psi vs reference")
+        assert_close_np(res.phi.cpu().numpy(), g[f"phi_{key}"], RTOL, ATOL, "phi vs reference")
+        assert_close_np(res.psi.cpu().numpy(), g[f"psi_{key}"], RTOL, ATOL, "psi vs reference")
     else:
-        fin = np.isfinite(g[f"phi_{key}"])
-        c = float(np.mean(phi[fin].astype(np.float64) - g[f"phi_{key}"][fin]))
-        assert_close_np(phi - np.float32(c), g[f"phi_{key}"], RTOL, 1e-4, "centred phi vs reference")
-        assert_close_np(psi + np.float32(c), g[f"psi_{key}"], RTOL, 1e-4, "centred psi vs reference")
+        n, m = meta["n"], meta["m"]
+        P0 = np.zeros((n, m))
+        np.add.at(P0, (gr, gc), gS.astype(np.float64))
+        P1 = np.zeros((n, m))
+        np.add.at(P1, (res.rows.cpu().numpy(), res.cols.cpu().numpy()),
+                  res.S.cpu().numpy().astype(np.float64))
+        np.testing.assert_allclose(P1, P0, rtol=0, atol=1e-5)
 
 
 @pytest.mark.parametrize("variant", ["alternating", "symmetric"])
@@ -155,20 +161,30 @@ def test_full_size_alternating_matches_torch_reference_ops(cuda):
     a = torch.full((n,), 1.0 / n, device=cuda)
     res = sinkslot_solve(X, Y, a, a, 0.01, 64, 0, 500)
     lam, _ = cost_and_lam(X, Y, res.rows, res.cols, res.S, 0.01)
-    phi, psi = alternating_fixed(res.rows, res.cols, lam, a.log(), a.log(), n, n, 500)
-    # Raw per-element agreement: the rtol/atol bar holds except for potentials
-    # within ~1e-3 of zero, where the difference is the common (+c, -c) shift
-    # that 500 iterations accumulate from last-bit differences in exp/log; the
-    # reference's own backends differ from each other the same way.
+    la = a.log()
+    phi, psi = alternating_fixed(res.rows, res.cols, lam, la, la, n, n, 500)
+    # The same iteration in float64 on the same fp32 inputs: the exact answer
+    # both fp32 implementations approximate.
+    phi64, psi64 = alternating_fixed(res.rows, res.cols, lam.double(), la.double(), la.double(),
+                                     n, n, 500)
+    # Raw per-element agreement with the reference ops: the rtol/atol bar holds
+    # except for a handful of potentials near zero, where the difference is
+    # the common (+c, -c) shift that 500 iterations accumulate from last-bit
+    # differences in exp/log (undamped by Sinkhorn).
     d_phi = (res.phi - phi).double()
     d_psi = (res.psi - psi).double()
     bad = (d_phi.abs() > ATOL + RTOL * phi.abs()).sum() + (d_psi.abs() > ATOL + RTOL * psi.abs()).sum()
-    assert int(bad) <= 2e-4 * (2 * n), f"{int(bad)} potentials outside rtol/atol"
-    c = float(d_phi.mean())
-    assert abs(c) < 1e-3 and abs(float(d_psi.mean()) + c) < 1e-4
-    # after removing the shift, every element is within the bar
-    torch.testing.assert_close(res.phi - c, phi, rtol=RTOL, atol=ATOL)
-    torch.testing.assert_close(res.psi + c, psi, rtol=RTOL, atol=ATOL)
+    assert int(bad) <= 1e-4 * (2 * n), f"{int(bad)} potentials outside rtol/atol"
+    # Accuracy against the float64 answer is no worse than the reference's own
+    # fp32 implementation's (max and 99.9th percentile of |error|, within 2x).
+    for ours, ref, truth in ((res.phi, phi, phi64), (res.psi, psi, psi64)):
+        e_ours = (ours.double() - truth).abs()
+        e_ref = (ref.double() - truth).abs()
+        assert float(e_ours.max()) <= 2 * float(e_ref.max()) + 1e-6, \
+            f"max error {float(e_ours.max()):.3e} vs reference fp32 {float(e_ref.max()):.3e}"
+        q_ours = float(torch.quantile(e_ours[::16], 0.999))
+        q_ref = float(torch.quantile(e_ref[::16], 0.999))
+        assert q_ours <= 2 * q_ref + 1e-6, f"p99.9 error {q_ours:.3e} vs reference {q_ref:.3e}"
     # column marginal is exact after the column half-step (size-independent property)
     P = (res.phi[res.rows] + res.psi[res.cols] + lam).exp()
     col = torch.zeros(n, device=cuda, dtype=torch.float64).index_add_(0, res.cols, P.double())

@@ -108,8 +108,13 @@ def test_tiled_matches_exact_fixed(cuda, n, m, d, kind, eps, L, variant):
     pt, qt, *_ = fn(*csr, 150, tiles=tiles)
     pt2, qt2, *_ = fn(*csr, 150, tiles=tiles)
     assert torch.equal(pt, pt2) and torch.equal(qt, qt2), "tiled solve is not reproducible"
-    torch.testing.assert_close(pt, pe, rtol=RTOL, atol=ATOL)
-    torch.testing.assert_close(qt, qe, rtol=RTOL, atol=ATOL)
+    # Both are fp32 with different summation orders; after 150 iterations their
+    # difference near zero is the fp32 resolution of the potentials' scale
+    # (|phi| reaches ~10^3 at eps = 0.01), so atol is scaled by max|phi|.
+    atol_p = ATOL + 2e-7 * float(pe.abs().max())
+    atol_q = ATOL + 2e-7 * float(qe.abs().max())
+    torch.testing.assert_close(pt, pe, rtol=RTOL, atol=atol_p)
+    torch.testing.assert_close(qt, qe, rtol=RTOL, atol=atol_q)
 
 
 @pytest.mark.parametrize("mode,tol", [("marginal", 1e-6), ("potential", 1e-5)])
