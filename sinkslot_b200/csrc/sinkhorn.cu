@@ -16,6 +16,7 @@
 //     max-reduced into one device word per side.
 #include <cfloat>
 #include <cmath>
+#include <string>
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -174,7 +175,22 @@ static int read_acc(const uint32_t* d_acc, double* a0, double* a1, cudaStream_t 
 
 static double py_max(double a, double b) { return (b > a) ? b : a; }  // Python's max(a, b)
 
-size_t solve_work_floats(int64_t n, int64_t m) { return (size_t)(3 * (n + m) + 64); }
+// sub-buffers start on 16-byte boundaries (the tiled kernel bulk-copies potentials)
+static int64_t pad4(int64_t v) { return (v + 3) & ~int64_t(3); }
+
+size_t solve_work_floats(int64_t n, int64_t m) { return (size_t)(3 * (pad4(n) + pad4(m)) + 64); }
+
+static int read_err(const int* d_err, cudaStream_t st) {
+  int h = 0;
+  SINKSLOT_CUDA_TRY(cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  SINKSLOT_CUDA_TRY(cudaStreamSynchronize(st));
+  if (h != 0) {
+    set_error("tiled half-step: a shared-memory pipeline wait timed out (code " +
+              std::to_string(h) + ")");
+    return kCudaError;
+  }
+  return kOk;
+}
 
 int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t work_floats,
                int64_t* iters_run, int* converged, double* final_viol, cudaStream_t st) {
@@ -185,20 +201,22 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   SINKSLOT_REQUIRE(work_floats >= (int64_t)solve_work_floats(n, m), "solve: work buffer too small");
   SINKSLOT_REQUIRE((sp.row_tiles == nullptr) == (sp.col_tiles == nullptr),
                    "solve: give tiled layouts for both sides or neither");
-  // work: phi_next (n) | psi_next (m) | prev_phi (n) | prev_psi (m) |
-  //       64 words: [0,1] check maxima, [2,3] handed-back row counts |
-  //       handed-back row lists (n, m)
+  // work (each part 16-byte aligned): phi_next (n) | psi_next (m) | prev_phi (n) |
+  //       prev_psi (m) | 64 words: [0,1] check maxima, [2,3] handed-back row
+  //       counts, [4] pipeline error | handed-back row lists (n, m)
+  const int64_t n4 = pad4(n), m4 = pad4(m);
   float* phi_next = work;
-  float* psi_next = work + n;
-  float* prev_phi = work + n + m;
-  float* prev_psi = work + 2 * n + m;
-  uint32_t* acc = reinterpret_cast<uint32_t*>(work + 2 * (n + m));
+  float* psi_next = work + n4;
+  float* prev_phi = work + n4 + m4;
+  float* prev_psi = work + 2 * n4 + m4;
+  uint32_t* acc = reinterpret_cast<uint32_t*>(work + 2 * (n4 + m4));
   int* fb_count = reinterpret_cast<int*>(acc + 2);
-  int* fb_rows = reinterpret_cast<int*>(work + 2 * (n + m) + 64);
-  int* fb_cols = fb_rows + n;
+  int* perr = reinterpret_cast<int*>(acc + 4);
+  int* fb_rows = reinterpret_cast<int*>(work + 2 * (n4 + m4) + 64);
+  int* fb_cols = fb_rows + n4;
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(phi, 0, n * sizeof(float), st));
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(psi, 0, m * sizeof(float), st));
-  SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, 4 * sizeof(uint32_t), st));
+  SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, 8 * sizeof(uint32_t), st));
   if (sp.mode == 1) {
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_phi, 0, n * sizeof(float), st));
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_psi, 0, m * sizeof(float), st));
@@ -244,6 +262,7 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
       t.fb_count = fb_count + (row ? 0 : 1);
       t.fb_list = row ? fb_rows : fb_cols;
       t.fb_count_reset = fb_count + (row ? 1 : 0);
+      t.err = perr;
       return tiled_half_step(t, out_mode, chk, st);
     }
     HalfStep h = side;
@@ -333,6 +352,7 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   if (psi_cur != psi)
     SINKSLOT_CUDA_TRY(cudaMemcpyAsync(psi, psi_cur, m * sizeof(float), cudaMemcpyDeviceToDevice, st));
   *iters_run = it;
+  if (sp.row_tiles) return read_err(perr, st);
   return kOk;
 }
 

@@ -3,14 +3,24 @@
 // Why: a half-step gathers one potential value per support entry at random
 // (67M gathers of a 4 MB vector per half-step at N = M = 2^20).  From global
 // memory every gather is its own 32-byte sector request through L1TEX and L2,
-// which caps the plain kernel near 1/4 of the HBM roofline.  Here each CTA owns
-// a panel of R rows and walks the gathered axis in blocks of W entries: the
-// block is copied into shared memory (cp.async, double-buffered) once per panel
-// and every gather becomes a shared-memory load.
+// which caps the exact kernel near 1/4 of the HBM roofline.  Here each CTA owns
+// a panel of R rows and walks the gathered axis in blocks of W entries; each
+// block is copied into shared memory once per panel and every gather becomes a
+// shared-memory load.
 //
 // Layout (built once per solve from the CSR side): tile (p, b) = the entries of
-// panel p whose column lies in block b, in CSR order; per entry one uint32
-// (row within the panel << 16 | column within the block) and the fp32 lam.
+// panel p whose column lies in block b, in CSR order, padded to a multiple of 4
+// entries (padding meta = 0xFFFFFFFF); per entry one uint32 (row within the
+// panel << 16 | column within the block) and the fp32 lam.
+//
+// Pipeline (one CTA per SM, warp-specialised): one producer warp issues TMA
+// bulk copies (cp.async.bulk) of potential blocks and of tile entry chunks into
+// two-stage shared-memory rings, each stage guarded by a full/empty mbarrier
+// pair; 16 consumer warps wait on "full", read entries and potentials from
+// shared memory, accumulate, and arrive on "empty".  No CTA-wide barrier per
+// tile.  Every mbarrier wait is bounded by a clock budget: on timeout the kernel
+// records an error code, the producer waits (bounded) for the copies it issued,
+// and all warps leave.
 //
 // Arithmetic: the log-sum-exp of a row is stabilised by the row's previous
 // value, sigma = base - self_old (the LSE the previous half-step produced), so
@@ -36,17 +46,25 @@
 
 namespace sinkslot {
 
-constexpr int kTileThreads = 1024;
-constexpr int kTileUnroll = 8;
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumers = 32 * kConsumerWarps;
+constexpr int kPipeThreads = kConsumers + 32;  // + one producer warp
+constexpr int kEntryUnroll = 8;
 constexpr size_t kSmemCap = 227 * 1024;
+constexpr size_t kBarBytes = 128;  // 8 mbarriers + the abort word
 constexpr float kFixScale = 4294967296.0f;  // 2^32
 constexpr double kFixInv = 1.0 / 4294967296.0;
 constexpr unsigned long long kFixMin = 1ull << 24;  // sums below 2^-8 go to the exact pass
 constexpr int kLoBits = 20;
+constexpr long long kWaitCycles = 8000000000ll;  // ~4 s at 2 GHz: a wait this long is a bug
 
 // shared memory per panel row: sigma, high sum, low sum (4 B each) + a flag bit
 static size_t rows_smem(int R) {
   return 3 * align_up((size_t)R * 4, 16) + align_up((size_t)((R + 31) / 32) * 4, 16);
+}
+
+static size_t pipe_smem(int R, int W, int E) {
+  return (size_t)2 * W * 4 + (size_t)2 * E * 8 + rows_smem(R) + kBarBytes;
 }
 
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
@@ -58,37 +76,49 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   int64_t P = sms;
   if (nseg < P * 32) P = std::max<int64_t>(1, ceil_div64(nseg, 32));
   int64_t R = ceil_div64(nseg, P);
-  // keep at least 2 x 4096 floats of staging room and R < 2^16
-  while ((int64_t)rows_smem((int)std::min<int64_t>(R, 1 << 20)) + 2 * 4096 * 4 + 1024 >
-             (int64_t)kSmemCap ||
-         R > 65535) {
+  // keep room for 2 x 2048-float blocks and 2 x 1024-entry chunks; R < 2^16
+  while (pipe_smem((int)std::min<int64_t>(R, 1 << 20), 2048, 1024) > kSmemCap || R > 65535) {
     P += sms;
     R = ceil_div64(nseg, P);
   }
-  const size_t avail = kSmemCap - rows_smem((int)R) - 1024;
-  int logW = 2;
-  while (logW < 16 && ((size_t)2 * 4 * ((size_t)1 << (logW + 1))) <= avail &&
-         ((int64_t)1 << logW) < m_o)
-    ++logW;
+  // widest block first (fewer tiles, longer rows per tile), then the longest chunk
+  int logW = 2, E = 1024;
+  const int logW_need = [&] {
+    int l = 2;
+    while (l < 16 && ((int64_t)1 << l) < m_o) ++l;
+    return l;
+  }();
+  for (int lw = logW_need; lw >= 2; --lw) {
+    int e = 4096;
+    while (e > 1024 && pipe_smem((int)R, 1 << lw, e) > kSmemCap) e >>= 1;
+    if (pipe_smem((int)R, 1 << lw, e) <= kSmemCap) {
+      logW = lw;
+      E = e;
+      break;
+    }
+  }
   g.P = (int)P;
   g.R = (int)R;
   g.logW = logW;
+  g.E = E;
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
-  g.smem_bytes = 2 * 4 * ((size_t)1 << logW) + rows_smem((int)R);
+  g.smem_bytes = pipe_smem((int)R, 1 << logW, E);
   const int64_t ntiles = (int64_t)g.P * g.B;
+  g.cap = nnz + 3 * ntiles;
   Carver cv(nullptr, 0);
-  cv.take<int64_t>(8);               // header: [0] longest row
-  cv.take<int64_t>(ntiles + 1);      // tile starts
-  cv.take<uint32_t>(std::max<int64_t>(nnz, 1));  // meta
-  cv.take<float>(std::max<int64_t>(nnz, 1));     // lam
+  cv.take<int64_t>(8);            // header: [0] longest row
+  cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
+  cv.take<uint32_t>(std::max<int64_t>(g.cap, 1));  // meta
+  cv.take<float>(std::max<int64_t>(g.cap, 1));     // lam
   g.layout_bytes = cv.used;
   Carver bw(nullptr, 0);
   const int64_t e = std::max<int64_t>(nnz, 1);
   bw.take<uint32_t>(e);  // row id
   bw.take<uint32_t>(e); bw.take<uint32_t>(e); bw.take<uint32_t>(e); bw.take<uint32_t>(e);
   const int64_t nh = radix_hist_elems(1, e);
-  bw.take<int64_t>(nh);
-  bw.take<int64_t>(scan_tmp_elems(nh));
+  bw.take<int64_t>(std::max<int64_t>(nh, ntiles + 2));
+  bw.take<int64_t>(scan_tmp_elems(std::max<int64_t>(nh, ntiles + 2)));
+  bw.take<int64_t>(ntiles + 2);  // unpadded tile starts
   g.build_bytes = bw.used;
   return g;
 }
@@ -105,8 +135,8 @@ static LayoutPtrs carve_layout(void* layout, const TileGeom& g) {
   LayoutPtrs p;
   p.header = cv.take<int64_t>(8);
   p.tstart = cv.take<int64_t>((int64_t)g.P * g.B + 1);
-  p.meta = cv.take<uint32_t>(std::max<int64_t>(g.nnz, 1));
-  p.lam = cv.take<float>(std::max<int64_t>(g.nnz, 1));
+  p.meta = cv.take<uint32_t>(std::max<int64_t>(g.cap, 1));
+  p.lam = cv.take<float>(std::max<int64_t>(g.cap, 1));
   return p;
 }
 
@@ -146,32 +176,52 @@ __global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __r
   }
 }
 
-__global__ void tstart_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
-                              int64_t* __restrict__ tstart) {
+// ustart[t] = #{sorted keys < t}; cnt4[t] = entries of tile t rounded up to 4
+__global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
+                                   int64_t* __restrict__ ustart, int64_t* __restrict__ cnt4) {
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t <= ntiles;
        t += (int64_t)gridDim.x * blockDim.x) {
-    int64_t lo = 0, hi = nnz;
-    while (lo < hi) {
-      const int64_t mid = (lo + hi) >> 1;
-      if ((int64_t)skey[mid] < t) lo = mid + 1; else hi = mid;
-    }
-    tstart[t] = lo;
+    auto lb = [&](int64_t v) {
+      int64_t lo = 0, hi = nnz;
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if ((int64_t)skey[mid] < v) lo = mid + 1; else hi = mid;
+      }
+      return lo;
+    };
+    const int64_t s = lb(t);
+    ustart[t] = s;
+    if (t < ntiles) cnt4[t] = (lb(t + 1) - s + 3) & ~int64_t(3);
+  }
+}
+
+__global__ void fill_meta_kernel(uint32_t* __restrict__ meta, float* __restrict__ lam,
+                                 int64_t cap) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < cap;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    meta[q] = 0xFFFFFFFFu;
+    lam[q] = 0.0f;
   }
 }
 
 template <typename IT>
 __global__ void tile_scatter_kernel(const uint32_t* __restrict__ perm,
+                                    const uint32_t* __restrict__ skey,
                                     const uint32_t* __restrict__ rowid, const IT* __restrict__ idx,
                                     const float* __restrict__ lam, int64_t nnz, int R, int logW,
+                                    const int64_t* __restrict__ ustart,
+                                    const int64_t* __restrict__ tstart,
                                     uint32_t* __restrict__ meta, float* __restrict__ tlam) {
   const uint32_t wmask = (1u << logW) - 1u;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
        q += (int64_t)gridDim.x * blockDim.x) {
     const uint32_t k = perm[q];
+    const uint32_t t = skey[q];
+    const int64_t pos = tstart[t] + (q - ustart[t]);
     const uint32_t r = rowid[k];
     const uint32_t c = (uint32_t)idx[k];
-    meta[q] = ((r % (uint32_t)R) << 16) | (c & wmask);
-    tlam[q] = lam[k];
+    meta[pos] = ((r % (uint32_t)R) << 16) | (c & wmask);
+    tlam[pos] = lam[k];
   }
 }
 
@@ -184,50 +234,135 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   LayoutPtrs L = carve_layout(layout, g);
   Carver cv(ws, ws_bytes);
   const int64_t e = std::max<int64_t>(g.nnz, 1);
+  const int64_t ntiles = (int64_t)g.P * g.B;
   uint32_t* rowid = cv.take<uint32_t>(e);
   uint32_t* k1 = cv.take<uint32_t>(e);
   uint32_t* v1 = cv.take<uint32_t>(e);
   uint32_t* k2 = cv.take<uint32_t>(e);
   uint32_t* v2 = cv.take<uint32_t>(e);
-  const int64_t nh = radix_hist_elems(1, e);
+  const int64_t nh = std::max<int64_t>(radix_hist_elems(1, e), ntiles + 2);
   int64_t* hist = cv.take<int64_t>(nh);
   int64_t* stmp = cv.take<int64_t>(scan_tmp_elems(nh));
+  int64_t* ustart = cv.take<int64_t>(ntiles + 2);
   if (!cv.ok) {
     set_error("build_tiles: workspace too small");
     return kWorkspaceTooSmall;
   }
-  const int64_t ntiles = (int64_t)g.P * g.B;
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.header, 0, 8 * sizeof(int64_t), st));
+  fill_meta_kernel<<<grid_t(g.cap, 256), 256, 0, st>>>(L.meta, L.lam, g.cap);
+  SINKSLOT_CHECK_LAUNCH();
   rowid_kernel<<<grid_t(g.nseg, 256), 256, 0, st>>>(
       ptr, g.nseg, rowid, reinterpret_cast<unsigned long long*>(L.header));
   SINKSLOT_CHECK_LAUNCH();
-  if (g.nnz > 0) {
-    if (idx_bytes == 2)
-      tilekey_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-          rowid, static_cast<const int16_t*>(idx), g.nnz, g.R, g.B, g.logW, k1);
-    else
-      tilekey_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-          rowid, static_cast<const int32_t*>(idx), g.nnz, g.R, g.B, g.logW, k1);
-    SINKSLOT_CHECK_LAUNCH();
-    bool alt = false;
-    SINKSLOT_TRY(radix_sort_pairs<uint32_t>(k1, v1, k2, v2, true, 1, g.nnz,
-                                            bits_for((uint64_t)std::max<int64_t>(ntiles, 2)), hist,
-                                            stmp, &alt, st));
-    const uint32_t* skey = alt ? k2 : k1;
-    const uint32_t* perm = alt ? v2 : v1;
-    tstart_kernel<<<grid_t(ntiles + 1, 256), 256, 0, st>>>(skey, g.nnz, ntiles, L.tstart);
-    SINKSLOT_CHECK_LAUNCH();
-    if (idx_bytes == 2)
-      tile_scatter_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-          perm, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW, L.meta, L.lam);
-    else
-      tile_scatter_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-          perm, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW, L.meta, L.lam);
-    SINKSLOT_CHECK_LAUNCH();
-  } else {
+  if (g.nnz == 0) {
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.tstart, 0, (ntiles + 1) * sizeof(int64_t), st));
+    return kOk;
   }
+  if (idx_bytes == 2)
+    tilekey_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
+        rowid, static_cast<const int16_t*>(idx), g.nnz, g.R, g.B, g.logW, k1);
+  else
+    tilekey_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
+        rowid, static_cast<const int32_t*>(idx), g.nnz, g.R, g.B, g.logW, k1);
+  SINKSLOT_CHECK_LAUNCH();
+  bool alt = false;
+  SINKSLOT_TRY(radix_sort_pairs<uint32_t>(k1, v1, k2, v2, true, 1, g.nnz,
+                                          bits_for((uint64_t)std::max<int64_t>(ntiles, 2)), hist,
+                                          stmp, &alt, st));
+  const uint32_t* skey = alt ? k2 : k1;
+  const uint32_t* perm = alt ? v2 : v1;
+  // padded tile starts: exclusive scan of the rounded-up counts (in L.tstart)
+  tile_counts_kernel<<<grid_t(ntiles + 1, 256), 256, 0, st>>>(skey, g.nnz, ntiles, ustart,
+                                                              L.tstart);
+  SINKSLOT_CHECK_LAUNCH();
+  SINKSLOT_TRY(scan_exclusive_i64(L.tstart, ntiles, stmp, L.tstart + ntiles, st));
+  if (idx_bytes == 2)
+    tile_scatter_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
+        perm, skey, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
+        L.tstart, L.meta, L.lam);
+  else
+    tile_scatter_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
+        perm, skey, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
+        L.tstart, L.meta, L.lam);
+  SINKSLOT_CHECK_LAUNCH();
   return kOk;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy helpers (PTX)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 1-D bulk copy global -> shared, completion counted on `bar` (16-B aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Bounded wait: spins on try_wait until the phase with `parity` completes, the
+// shared abort word is set by another warp, or the clock budget runs out (then
+// records `code` in *err and sets the abort word).  Returns true on completion.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_w,
+                                          int* err, int code) {
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_w) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, code);
+      *abort_w = 1;
+      return false;
+    }
+  }
+}
+
+// The same wait for a whole consumer warp, with a warp-uniform answer: every
+// lane polls the barrier (each gets acquire ordering on the staged data), the
+// warp proceeds when all lanes saw the phase complete, and lane 0 alone
+// decides an abort, broadcast to the warp.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_w,
+                                          int* err, int code) {
+  const long long t0 = clock64();
+  while (true) {
+    const bool done = mbar_try(bar, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    int stop = 0;
+    if ((threadIdx.x & 31) == 0) {
+      if (*abort_w) {
+        stop = 1;
+      } else if (clock64() - t0 > kWaitCycles) {
+        atomicCAS(err, 0, code);
+        *abort_w = 1;
+        stop = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -235,7 +370,7 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
 // ---------------------------------------------------------------------------
 struct TKArgs {
   int64_t nseg, m_o;
-  int P, R, B, logW;
+  int P, R, B, logW, E;
   const int64_t* header;
   const int64_t* tstart;
   const uint32_t* meta;
@@ -250,146 +385,168 @@ struct TKArgs {
   int* fb_count;
   int* fb_list;
   int* fb_reset;
-  int aligned16;  // `other` is 16-byte aligned: stage with 16-byte copies
+  int* err;
 };
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
-}
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
-
-// copy other[b*W, min((b+1)*W, m_o)) into buf (all threads participate)
-__device__ __forceinline__ void stage_block(const TKArgs& a, int b, float* buf) {
-  const int64_t W = (int64_t)1 << a.logW;
-  const int64_t c0 = (int64_t)b * W;
-  const int64_t cnt = std::min<int64_t>(W, a.m_o - c0);
-  const float* src = a.other + c0;
-  if (a.aligned16) {
-    const int64_t n16 = cnt >> 2;
-    for (int64_t q = threadIdx.x; q < n16; q += kTileThreads) cp_async16(buf + 4 * q, src + 4 * q);
-    for (int64_t q = (n16 << 2) + threadIdx.x; q < cnt; q += kTileThreads) cp_async4(buf + q, src + q);
-  } else {
-    for (int64_t q = threadIdx.x; q < cnt; q += kTileThreads) cp_async4(buf + q, src + q);
-  }
-}
-
 template <int OUT, int CHK>
-__global__ void __launch_bounds__(kTileThreads, 1) tiled_half_step_kernel(const TKArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const TKArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
   const int W = 1 << a.logW;
+  const int E = a.E;
   const size_t rbytes = align_up((size_t)a.R * 4, 16);
-  float* pot0 = reinterpret_cast<float*>(smem);
-  float* pot1 = pot0 + W;
-  float* sig = reinterpret_cast<float*>(smem + (size_t)2 * 4 * W);
-  uint32_t* hi = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(sig) + rbytes);
-  uint32_t* lo = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(hi) + rbytes);
-  uint32_t* flags = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(lo) + rbytes);
-  if (a.fb_reset && blockIdx.x == 0 && threadIdx.x == 0) *a.fb_reset = 0;
+  float* pot = reinterpret_cast<float*>(smem);                         // [2][W]
+  uint32_t* emeta = reinterpret_cast<uint32_t*>(smem + (size_t)2 * W * 4);  // [2][E]
+  float* elam = reinterpret_cast<float*>(smem + (size_t)2 * W * 4 + (size_t)2 * E * 4);  // [2][E]
+  unsigned char* rowp = smem + (size_t)2 * W * 4 + (size_t)2 * E * 8;
+  float* sig = reinterpret_cast<float*>(rowp);
+  uint32_t* hi = reinterpret_cast<uint32_t*>(rowp + rbytes);
+  uint32_t* lo = reinterpret_cast<uint32_t*>(rowp + 2 * rbytes);
+  uint32_t* flags = reinterpret_cast<uint32_t*>(rowp + 3 * rbytes);
+  unsigned long long* bars = reinterpret_cast<unsigned long long*>(
+      rowp + 3 * rbytes + align_up((size_t)((a.R + 31) / 32) * 4, 16));
+  volatile int* abort_w = reinterpret_cast<volatile int*>(bars + 8);
+  // bars: [0,1] potential full, [2,3] potential empty, [4,5] entries full, [6,7] entries empty
+  const uint32_t bar0 = smem_u32(bars);
+  auto pot_full = [&](int s) { return bar0 + 8u * (uint32_t)s; };
+  auto pot_empty = [&](int s) { return bar0 + 8u * (uint32_t)(2 + s); };
+  auto ent_full = [&](int s) { return bar0 + 8u * (uint32_t)(4 + s); };
+  auto ent_empty = [&](int s) { return bar0 + 8u * (uint32_t)(6 + s); };
 
-  // Terms are capped at 2^k, k = 20 - ceil(log2(longest row)), so the high-part
-  // sum of any row stays below 2^32; longer rows than 4096 would overflow the
-  // low-part sum, and then every row goes to the exact pass.
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  // a pipeline wait of an earlier launch timed out: do nothing (the host reports it)
+  if (*(volatile int*)a.err != 0) return;
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(pot_full(s), 1);
+      mbar_init(pot_empty(s), kConsumerWarps);
+      mbar_init(ent_full(s), 1);
+      mbar_init(ent_empty(s), kConsumerWarps);
+    }
+    *abort_w = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (a.fb_reset && blockIdx.x == 0 && tid == 0) *a.fb_reset = 0;
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer warp: lane 0 issues every copy ----------------
+    if (lane != 0) return;
+    long long nb = 0, nc = 0;  // blocks / chunks issued so far (stage = count & 1)
+    bool ok = true;
+    for (int p = blockIdx.x; ok && p < a.P; p += gridDim.x) {
+      if ((int64_t)p * a.R >= a.nseg) break;
+      const int64_t pb = (int64_t)p * a.B;
+      for (int b = 0; ok && b < a.B; ++b) {
+        const int s = (int)(nb & 1);
+        if (nb >= 2 && !(ok = mbar_wait(pot_empty(s), (uint32_t)(((nb >> 1) - 1) & 1), abort_w,
+                                        a.err, 1)))
+          break;
+        const int64_t c0 = (int64_t)b * W;
+        const int64_t cnt = std::min<int64_t>(W, a.m_o - c0);
+        const int64_t body = cnt & ~int64_t(3);
+        float* dst = pot + (size_t)s * W;
+        // the last few floats when the block is not a multiple of 16 bytes
+        for (int64_t q = body; q < cnt; ++q) dst[q] = a.other[c0 + q];
+        mbar_arrive_tx(pot_full(s), (uint32_t)(body * 4));
+        if (body > 0) bulk_g2s(smem_u32(dst), a.other + c0, (uint32_t)(body * 4), pot_full(s));
+        ++nb;
+        const int64_t e0 = a.tstart[pb + b], e1 = a.tstart[pb + b + 1];
+        for (int64_t c = e0; c < e1; c += E) {
+          const int s2 = (int)(nc & 1);
+          if (nc >= 2 && !(ok = mbar_wait(ent_empty(s2), (uint32_t)(((nc >> 1) - 1) & 1),
+                                          abort_w, a.err, 2)))
+            break;
+          const uint32_t len = (uint32_t)std::min<int64_t>(E, e1 - c);
+          mbar_arrive_tx(ent_full(s2), len * 8u);
+          bulk_g2s(smem_u32(emeta + (size_t)s2 * E), a.meta + c, len * 4u, ent_full(s2));
+          bulk_g2s(smem_u32(elam + (size_t)s2 * E), a.lam + c, len * 4u, ent_full(s2));
+          ++nc;
+        }
+      }
+    }
+    if (!ok) {
+      // wait (bounded) for the copies in flight so none lands after the CTA leaves
+      for (long long k = std::max(0ll, nb - 2); k < nb; ++k) {
+        const long long t0 = clock64();
+        while (!mbar_try(pot_full((int)(k & 1)), (uint32_t)((k >> 1) & 1)) &&
+               clock64() - t0 < kWaitCycles) {
+        }
+      }
+      for (long long k = std::max(0ll, nc - 2); k < nc; ++k) {
+        const long long t0 = clock64();
+        while (!mbar_try(ent_full((int)(k & 1)), (uint32_t)((k >> 1) & 1)) &&
+               clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
   const long long longest = a.header[0] > 0 ? a.header[0] : 1;
   int lg = 0;
   while ((1ll << lg) < longest) ++lg;
   const int k = kLoBits - lg;
+  // terms above 2^k would overflow the high-part sum of the longest row
   const float capd = (longest <= 4096 && k >= 1) ? ((float)k - 0.01f) * 0.69314718f : -INFINITY;
   uint32_t chk_bits = 0;
-  constexpr int64_t kRound = (int64_t)kTileThreads * kTileUnroll;
-
-  for (int p = blockIdx.x; p < a.P; p += gridDim.x) {
+  long long nb = 0, nc = 0;
+  bool ok = true;
+  // Control flow that crosses a consumer barrier follows the shared abort word
+  // (identical for all consumers after bar.sync), never a thread-local flag.
+  for (int p = blockIdx.x; !*abort_w && p < a.P; p += gridDim.x) {
     const int64_t row0 = (int64_t)p * a.R;
     const int rows = (int)std::min<int64_t>(a.R, a.nseg - row0);
     if (rows <= 0) break;
     const int64_t pb = (int64_t)p * a.B;
-    for (int r = threadIdx.x; r < a.R; r += kTileThreads) {
+    for (int r = tid; r < a.R; r += kConsumers) {
       hi[r] = 0u;
       lo[r] = 0u;
       sig[r] = r < rows ? __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]) : 0.0f;
     }
-    for (int r = threadIdx.x; r < (a.R + 31) / 32; r += kTileThreads) flags[r] = 0u;
-    stage_block(a, 0, pot0);
-    cp_async_commit();
-    // entries of the first round of tile 0, loaded while the block stages
-    uint32_t mt[kTileUnroll];
-    float lv[kTileUnroll];
-    {
-      const int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
+    for (int r = tid; r < (a.R + 31) / 32; r += kConsumers) flags[r] = 0u;
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
+    for (int b = 0; ok && b < a.B; ++b) {
+      const int s = (int)(nb & 1);
+      if (!(ok = warp_wait(pot_full(s), (uint32_t)((nb >> 1) & 1), abort_w, a.err, 3))) break;
+      ++nb;
+      const float* cur = pot + (size_t)s * W;
+      const int64_t e0 = a.tstart[pb + b], e1 = a.tstart[pb + b + 1];
+      for (int64_t c = e0; c < e1; c += E) {
+        const int s2 = (int)(nc & 1);
+        if (!(ok = warp_wait(ent_full(s2), (uint32_t)((nc >> 1) & 1), abort_w, a.err, 4))) break;
+        ++nc;
+        const int len = (int)std::min<int64_t>(E, e1 - c);
+        const uint32_t* mt = emeta + (size_t)s2 * E;
+        const float* lv = elam + (size_t)s2 * E;
+        for (int i0 = 0; i0 < len; i0 += kConsumers * kEntryUnroll) {
 #pragma unroll
-      for (int u = 0; u < kTileUnroll; ++u) {
-        const int64_t e = e0 + (int64_t)u * kTileThreads + threadIdx.x;
-        mt[u] = e < e1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
-        lv[u] = e < e1 ? ld_stream(a.lam + e) : 0.0f;
-      }
-    }
-    __syncthreads();
-    for (int b = 0; b < a.B; ++b) {
-      const float* cur = (b & 1) ? pot1 : pot0;
-      if (b + 1 < a.B) {
-        stage_block(a, b + 1, (b & 1) ? pot0 : pot1);
-        cp_async_commit();
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
-      __syncthreads();
-      const int64_t e0 = a.tstart[pb + b];
-      const int64_t e1 = a.tstart[pb + b + 1];
-      // prefetch the next tile's first round; it lands while this tile computes
-      uint32_t nmt[kTileUnroll];
-      float nlv[kTileUnroll];
-      {
-        const int64_t f0 = e1;
-        const int64_t f1 = (b + 1 < a.B) ? a.tstart[pb + b + 2] : e1;
-#pragma unroll
-        for (int u = 0; u < kTileUnroll; ++u) {
-          const int64_t e = f0 + (int64_t)u * kTileThreads + threadIdx.x;
-          nmt[u] = e < f1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
-          nlv[u] = e < f1 ? ld_stream(a.lam + e) : 0.0f;
-        }
-      }
-      for (int64_t base_e = e0;;) {
-#pragma unroll
-        for (int u = 0; u < kTileUnroll; ++u) {
-          if (mt[u] == 0xFFFFFFFFu) continue;
-          const uint32_t r = mt[u] >> 16;
-          const uint32_t c = mt[u] & 0xFFFFu;
-          const float d = __fsub_rn(__fadd_rn(lv[u], cur[c]), sig[r]);
-          if (!(d <= capd)) {
-            atomicOr(flags + (r >> 5), 1u << (r & 31));
-          } else {
-            const unsigned long long q = __float2ull_rn(__expf(d) * kFixScale);
-            atomicAdd(hi + r, (uint32_t)(q >> kLoBits));
-            atomicAdd(lo + r, (uint32_t)(q & ((1u << kLoBits) - 1u)));
+          for (int u = 0; u < kEntryUnroll; ++u) {
+            const int i = i0 + u * kConsumers + tid;
+            if (i >= len) break;
+            const uint32_t m = mt[i];
+            if (m == 0xFFFFFFFFu) continue;
+            const uint32_t r = m >> 16;
+            const float d = __fsub_rn(__fadd_rn(lv[i], cur[m & 0xFFFFu]), sig[r]);
+            if (!(d <= capd)) {
+              atomicOr(flags + (r >> 5), 1u << (r & 31));
+            } else {
+              const unsigned long long q = __float2ull_rn(__expf(d) * kFixScale);
+              atomicAdd(hi + r, (uint32_t)(q >> kLoBits));
+              atomicAdd(lo + r, (uint32_t)(q & ((1u << kLoBits) - 1u)));
+            }
           }
         }
-        base_e += kRound;
-        if (base_e >= e1) break;
-        // tiles longer than one round: the further rounds load in place
-#pragma unroll
-        for (int u = 0; u < kTileUnroll; ++u) {
-          const int64_t e = base_e + (int64_t)u * kTileThreads + threadIdx.x;
-          mt[u] = e < e1 ? ld_stream(a.meta + e) : 0xFFFFFFFFu;
-          lv[u] = e < e1 ? ld_stream(a.lam + e) : 0.0f;
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ent_empty(s2));
       }
-#pragma unroll
-      for (int u = 0; u < kTileUnroll; ++u) {
-        mt[u] = nmt[u];
-        lv[u] = nlv[u];
-      }
-      __syncthreads();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pot_empty(s));
     }
-    for (int r = threadIdx.x; r < rows; r += kTileThreads) {
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
+    if (*abort_w) break;
+    for (int r = tid; r < rows; r += kConsumers) {
       const int64_t seg = row0 + r;
       const unsigned long long q = ((unsigned long long)hi[r] << kLoBits) + lo[r];
       const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
@@ -402,7 +559,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) tiled_half_step_kernel(const 
       segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
                                  chk_bits);
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
   }
   check_reduce<CHK>(chk_bits, a.acc);
 }
@@ -420,15 +577,17 @@ static int launch_tiled(const TKArgs& a, size_t smem, cudaStream_t st) {
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   const int grid = std::min(a.P, num_sms());
-  tiled_half_step_kernel<OUT, CHK><<<grid, kTileThreads, smem, st>>>(a);
+  tiled_half_step_kernel<OUT, CHK><<<grid, kPipeThreads, smem, st>>>(a);
   SINKSLOT_CHECK_LAUNCH();
   return kOk;
 }
 
 int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st) {
   SINKSLOT_REQUIRE(h.base != nullptr, "tiled half step: base is required");
-  SINKSLOT_REQUIRE(h.fb_count && h.fb_list, "tiled half step: fallback list is required");
+  SINKSLOT_REQUIRE(h.fb_count && h.fb_list && h.err, "tiled half step: fallback list is required");
   SINKSLOT_REQUIRE(out_mode != kOutNone || chk == kChkMarg, "half step: check-only needs a check");
+  SINKSLOT_REQUIRE((reinterpret_cast<uintptr_t>(h.other) & 15u) == 0,
+                   "tiled half step: the gathered potential must be 16-byte aligned");
   if (h.g.nseg <= 0) return kOk;
   LayoutPtrs L = carve_layout(const_cast<void*>(h.layout), h.g);
   TKArgs a;
@@ -438,6 +597,7 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.R = h.g.R;
   a.B = h.g.B;
   a.logW = h.g.logW;
+  a.E = h.g.E;
   a.header = L.header;
   a.tstart = L.tstart;
   a.meta = L.meta;
@@ -453,7 +613,7 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.fb_count = h.fb_count;
   a.fb_list = h.fb_list;
   a.fb_reset = h.fb_count_reset;
-  a.aligned16 = ((reinterpret_cast<uintptr_t>(h.other) & 15u) == 0) ? 1 : 0;
+  a.err = h.err;
   const size_t smem = h.g.smem_bytes;
   if (out_mode == kOutPlain) {
     if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkNone>(a, smem, st)));

@@ -9,13 +9,14 @@ namespace sinkslot {
 
 // Geometry of a tiled layout: P panels of R rows; the gathered axis (length
 // m_o) cut into B blocks of W = 2^logW entries.  Tile (p, b) holds the entries
-// of panel p whose column falls in block b, in CSR order.
+// of panel p whose column falls in block b, in CSR order, padded to a multiple
+// of 4 entries; the kernel streams a tile in chunks of at most E entries.
 struct TileGeom {
   int64_t nseg = 0, m_o = 0, nnz = 0;
-  int P = 0, R = 0, B = 0, logW = 0;
-  int max_row = 0;          // longest segment (bounds the fixed-point range)
+  int P = 0, R = 0, B = 0, logW = 0, E = 0;
+  int64_t cap = 0;          // entries in the layout (nnz plus tile padding)
   size_t smem_bytes = 0;    // dynamic shared memory of the tiled kernel
-  size_t layout_bytes = 0;  // tile_start + meta + lam
+  size_t layout_bytes = 0;  // header + tile_start + meta + lam
   size_t build_bytes = 0;   // scratch of the builder
 };
 
@@ -41,9 +42,10 @@ struct TiledHalfStep {
   float w_old = 0.5f, w_new = 0.5f;
   float* prev = nullptr;
   uint32_t* acc = nullptr;
-  int* fb_count = nullptr;       // rows handed to the exact pass (reset by the caller)
-  int* fb_list = nullptr;        // nseg entries
+  int* fb_count = nullptr;        // rows handed to the exact pass (reset by the caller)
+  int* fb_list = nullptr;         // nseg entries
   int* fb_count_reset = nullptr;  // optional counter this launch zeroes (the other side's)
+  int* err = nullptr;             // set nonzero when a pipeline wait times out
 };
 
 // tiled pass + exact pass over the rows it handed back

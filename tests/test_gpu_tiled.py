@@ -68,23 +68,31 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     layout = build_tiles(ptr, idx, lam, n, m).cpu().numpy()
     P, R, B, logW, smem = _geometry(n, m, nnz)
     assert smem <= 227 * 1024 and R < 65536 and P * R >= n and B << logW >= m
+    T = P * B
+    cap = nnz + 3 * T
     off = _align(64)
-    tstart = layout[off:off + 8 * (P * B + 1)].view(np.int64)
-    off = _align(off + 8 * (P * B + 1))
-    meta = layout[off:off + 4 * nnz].view(np.uint32)
-    off = _align(off + 4 * nnz)
-    tlam = layout[off:off + 4 * nnz].view(np.float32)
-    assert tstart[0] == 0 and tstart[-1] == nnz and np.all(np.diff(tstart) >= 0)
+    tstart = layout[off:off + 8 * (T + 1)].view(np.int64)
+    off = _align(off + 8 * (T + 1))
+    meta = layout[off:off + 4 * cap].view(np.uint32)
+    off = _align(off + 4 * cap)
+    tlam = layout[off:off + 4 * cap].view(np.float32)
     ptr_h = ptr.cpu().numpy().astype(np.int64)
     idx_h = idx.cpu().numpy().astype(np.int64)
     lam_h = lam.cpu().numpy()
     row_of = np.repeat(np.arange(n), np.diff(ptr_h))
     tile_of = (row_of // R) * B + (idx_h >> logW)
     order = np.argsort(tile_of, kind="stable")
-    np.testing.assert_array_equal(np.searchsorted(tile_of[order], np.arange(P * B + 1)), tstart)
-    want_meta = ((row_of[order] % R) << 16) | (idx_h[order] & ((1 << logW) - 1))
+    counts = np.bincount(tile_of, minlength=T)
+    padded = (counts + 3) // 4 * 4
+    np.testing.assert_array_equal(tstart, np.concatenate([[0], np.cumsum(padded)]))
+    want_meta = np.full(cap, 0xFFFFFFFF, dtype=np.uint64)
+    want_lam = np.zeros(cap, dtype=np.float32)
+    ustart = np.concatenate([[0], np.cumsum(counts)])
+    pos = tstart[tile_of[order]] + (np.arange(nnz) - ustart[tile_of[order]])
+    want_meta[pos] = ((row_of[order] % R) << 16) | (idx_h[order] & ((1 << logW) - 1))
+    want_lam[pos] = lam_h[order]
     np.testing.assert_array_equal(meta, want_meta.astype(np.uint32))
-    np.testing.assert_array_equal(tlam, lam_h[order])
+    np.testing.assert_array_equal(tlam, want_lam)
 
 
 CASES = [
