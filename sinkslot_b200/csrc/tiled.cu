@@ -16,7 +16,7 @@
 // Pipeline (one CTA per SM, warp-specialised): one producer warp issues TMA
 // bulk copies (cp.async.bulk) of potential blocks and of tile entry chunks into
 // two-stage shared-memory rings, each stage guarded by a full/empty mbarrier
-// pair; 16 consumer warps wait on "full", read entries and potentials from
+// pair; 31 consumer warps wait on "full", read entries and potentials from
 // shared memory, accumulate, and arrive on "empty".  No CTA-wide barrier per
 // tile.  Every mbarrier wait is bounded by a clock budget: on timeout the kernel
 // records an error code, the producer waits (bounded) for the copies it issued,
@@ -46,7 +46,7 @@
 
 namespace sinkslot {
 
-constexpr int kConsumerWarps = 16;
+constexpr int kConsumerWarps = 31;  // + 1 producer warp = 1024 threads
 constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kPipeThreads = kConsumers + 32;  // + one producer warp
 constexpr int kEntryUnroll = 8;

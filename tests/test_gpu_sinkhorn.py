@@ -185,10 +185,13 @@ def test_full_size_alternating_matches_torch_reference_ops(cuda):
         q_ours = float(torch.quantile(e_ours[::16], 0.999))
         q_ref = float(torch.quantile(e_ref[::16], 0.999))
         assert q_ours <= 2 * q_ref + 1e-6, f"p99.9 error {q_ours:.3e} vs reference {q_ref:.3e}"
-    # column marginal is exact after the column half-step (size-independent property)
+    # The column marginal is exact after the column half-step (a size-independent
+    # property), up to fp32 rounding of the exponent: phi + psi + lam cancels
+    # potentials of magnitude ~2e3 (ulp 1.2e-4) down to O(1), so plan entries
+    # carry ~1e-4 relative noise.
     P = (res.phi[res.rows] + res.psi[res.cols] + lam).exp()
     col = torch.zeros(n, device=cuda, dtype=torch.float64).index_add_(0, res.cols, P.double())
-    torch.testing.assert_close(col, a.double(), rtol=1e-4, atol=0)
+    torch.testing.assert_close(col, a.double(), rtol=1e-3, atol=0)
 
 
 def test_deterministic_and_auto_equals_b200(cuda):
