@@ -70,7 +70,9 @@ inline int num_sms() {
 
 __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-__host__ __device__ inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+__host__ __device__ constexpr inline size_t align_up(size_t x, size_t a = 256) {
+  return (x + a - 1) / a * a;
+}
 
 // Bump allocator over a caller-provided workspace.  Every carve is 256-byte
 // aligned; `ok` turns false when the workspace is too small.

@@ -15,7 +15,7 @@
 //
 // Pipeline (one CTA per SM, warp-specialised): one producer warp issues TMA
 // bulk copies (cp.async.bulk) of potential blocks and of tile entry chunks into
-// two-stage shared-memory rings, each stage guarded by a full/empty mbarrier
+// shared-memory rings of kStages stages, each stage guarded by a full/empty mbarrier
 // pair; 31 consumer warps wait on "full", read entries and potentials from
 // shared memory, accumulate, and arrive on "empty".  No CTA-wide barrier per
 // tile.  Every mbarrier wait is bounded by a clock budget: on timeout the kernel
@@ -51,7 +51,23 @@ constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kPipeThreads = kConsumers + 32;  // + one producer warp
 constexpr int kEntryUnroll = 8;
 constexpr size_t kSmemCap = 227 * 1024;
-constexpr size_t kBarBytes = 128;  // 8 mbarriers + the abort word
+
+// Build-time tuning of the pipeline (defaults measured on B200):
+//   SINKSLOT_TILE_STAGES   ring depth of both the potential and the entry ring
+//   SINKSLOT_TILE_ROWS_KB  budget for the per-row state; more panels than SMs
+//                          are used (each SM walks several) to stay within it
+//   SINKSLOT_TILE_MAX_LOGW widest potential block (2^x floats)
+#ifndef SINKSLOT_TILE_STAGES
+#define SINKSLOT_TILE_STAGES 3
+#endif
+#ifndef SINKSLOT_TILE_ROWS_KB
+#define SINKSLOT_TILE_ROWS_KB 48
+#endif
+#ifndef SINKSLOT_TILE_MAX_LOGW
+#define SINKSLOT_TILE_MAX_LOGW 14
+#endif
+constexpr int kStages = SINKSLOT_TILE_STAGES;
+constexpr size_t kBarBytes = align_up(32 * kStages + 16, 128);  // 4 mbarriers per stage + abort
 constexpr float kFixScale = 4294967296.0f;  // 2^32
 constexpr double kFixInv = 1.0 / 4294967296.0;
 constexpr unsigned long long kFixMin = 1ull << 24;  // sums below 2^-8 go to the exact pass
@@ -64,7 +80,7 @@ static size_t rows_smem(int R) {
 }
 
 static size_t pipe_smem(int R, int W, int E) {
-  return (size_t)2 * W * 4 + (size_t)2 * E * 8 + rows_smem(R) + kBarBytes;
+  return (size_t)kStages * ((size_t)W * 4 + (size_t)E * 8) + rows_smem(R) + kBarBytes;
 }
 
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
@@ -76,21 +92,28 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   int64_t P = sms;
   if (nseg < P * 32) P = std::max<int64_t>(1, ceil_div64(nseg, 32));
   int64_t R = ceil_div64(nseg, P);
-  // keep room for 2 x 2048-float blocks and 2 x 1024-entry chunks; R < 2^16
-  while (pipe_smem((int)std::min<int64_t>(R, 1 << 20), 2048, 1024) > kSmemCap || R > 65535) {
+  // per-row state within its budget (more panels per SM), R < 2^16, and room
+  // for the smallest rings
+  const size_t rows_budget = (size_t)SINKSLOT_TILE_ROWS_KB * 1024;
+  while ((rows_smem((int)std::min<int64_t>(R, 1 << 20)) > rows_budget && R > 32) || R > 65535 ||
+         pipe_smem((int)std::min<int64_t>(R, 1 << 20), 256, 256) > kSmemCap) {
     P += sms;
     R = ceil_div64(nseg, P);
   }
-  // widest block first (fewer tiles, longer rows per tile), then the longest chunk
-  int logW = 2, E = 1024;
+  // widest block first (fewer tiles); the entry chunk sized to hold a typical
+  // tile (256..4096 entries), shrunk if the rings do not fit
   const int logW_need = [&] {
     int l = 2;
-    while (l < 16 && ((int64_t)1 << l) < m_o) ++l;
+    while (l < SINKSLOT_TILE_MAX_LOGW && ((int64_t)1 << l) < m_o) ++l;
     return l;
   }();
+  int logW = 2, E = 256;
   for (int lw = logW_need; lw >= 2; --lw) {
-    int e = 4096;
-    while (e > 1024 && pipe_smem((int)R, 1 << lw, e) > kSmemCap) e >>= 1;
+    const int64_t B = ceil_div64(m_o, (int64_t)1 << lw);
+    int64_t want = ceil_div64(std::max<int64_t>(nnz, 1), P * B);
+    want = std::min<int64_t>(4096, std::max<int64_t>(256, (want + 255) / 256 * 256));
+    int e = (int)want;
+    while (e > 256 && pipe_smem((int)R, 1 << lw, e) > kSmemCap) e -= 256;
     if (pipe_smem((int)R, 1 << lw, e) <= kSmemCap) {
       logW = lw;
       E = e;
@@ -394,30 +417,31 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   const int W = 1 << a.logW;
   const int E = a.E;
   const size_t rbytes = align_up((size_t)a.R * 4, 16);
-  float* pot = reinterpret_cast<float*>(smem);                         // [2][W]
-  uint32_t* emeta = reinterpret_cast<uint32_t*>(smem + (size_t)2 * W * 4);  // [2][E]
-  float* elam = reinterpret_cast<float*>(smem + (size_t)2 * W * 4 + (size_t)2 * E * 4);  // [2][E]
-  unsigned char* rowp = smem + (size_t)2 * W * 4 + (size_t)2 * E * 8;
+  // [kStages][W] potential blocks, [kStages][E] entry metas, [kStages][E] entry lams
+  float* pot = reinterpret_cast<float*>(smem);
+  uint32_t* emeta = reinterpret_cast<uint32_t*>(smem + (size_t)kStages * W * 4);
+  float* elam = reinterpret_cast<float*>(smem + (size_t)kStages * W * 4 + (size_t)kStages * E * 4);
+  unsigned char* rowp = smem + (size_t)kStages * ((size_t)W * 4 + (size_t)E * 8);
   float* sig = reinterpret_cast<float*>(rowp);
   uint32_t* hi = reinterpret_cast<uint32_t*>(rowp + rbytes);
   uint32_t* lo = reinterpret_cast<uint32_t*>(rowp + 2 * rbytes);
   uint32_t* flags = reinterpret_cast<uint32_t*>(rowp + 3 * rbytes);
   unsigned long long* bars = reinterpret_cast<unsigned long long*>(
       rowp + 3 * rbytes + align_up((size_t)((a.R + 31) / 32) * 4, 16));
-  volatile int* abort_w = reinterpret_cast<volatile int*>(bars + 8);
-  // bars: [0,1] potential full, [2,3] potential empty, [4,5] entries full, [6,7] entries empty
+  volatile int* abort_w = reinterpret_cast<volatile int*>(bars + 4 * kStages);
+  // bars, kStages each: potential full, potential empty, entries full, entries empty
   const uint32_t bar0 = smem_u32(bars);
   auto pot_full = [&](int s) { return bar0 + 8u * (uint32_t)s; };
-  auto pot_empty = [&](int s) { return bar0 + 8u * (uint32_t)(2 + s); };
-  auto ent_full = [&](int s) { return bar0 + 8u * (uint32_t)(4 + s); };
-  auto ent_empty = [&](int s) { return bar0 + 8u * (uint32_t)(6 + s); };
+  auto pot_empty = [&](int s) { return bar0 + 8u * (uint32_t)(kStages + s); };
+  auto ent_full = [&](int s) { return bar0 + 8u * (uint32_t)(2 * kStages + s); };
+  auto ent_empty = [&](int s) { return bar0 + 8u * (uint32_t)(3 * kStages + s); };
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   // a pipeline wait of an earlier launch timed out: do nothing (the host reports it)
   if (*(volatile int*)a.err != 0) return;
   if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(pot_full(s), 1);
       mbar_init(pot_empty(s), kConsumerWarps);
       mbar_init(ent_full(s), 1);
@@ -432,50 +456,53 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   if (warp == kConsumerWarps) {
     // ---------------- producer warp: lane 0 issues every copy ----------------
     if (lane != 0) return;
-    long long nb = 0, nc = 0;  // blocks / chunks issued so far (stage = count & 1)
+    // blocks / chunks issued so far; stage = count % kStages, use = count / kStages
+    long long nb = 0, nc = 0;
+    int sb = 0, sc = 0;          // current stage of each ring
+    uint32_t ub = 0, uc = 0;     // parity of the current use of that stage
     bool ok = true;
     for (int p = blockIdx.x; ok && p < a.P; p += gridDim.x) {
       if ((int64_t)p * a.R >= a.nseg) break;
       const int64_t pb = (int64_t)p * a.B;
+      int64_t e0 = a.tstart[pb], e1n = a.tstart[pb + 1];
       for (int b = 0; ok && b < a.B; ++b) {
-        const int s = (int)(nb & 1);
-        if (nb >= 2 && !(ok = mbar_wait(pot_empty(s), (uint32_t)(((nb >> 1) - 1) & 1), abort_w,
-                                        a.err, 1)))
-          break;
+        const int64_t e1 = e1n;
+        // next tile's end: loaded now, used after this tile's waits
+        if (b + 1 < a.B) e1n = a.tstart[pb + b + 2];
+        if (nb >= kStages && !(ok = mbar_wait(pot_empty(sb), ub ^ 1u, abort_w, a.err, 1))) break;
         const int64_t c0 = (int64_t)b * W;
         const int64_t cnt = std::min<int64_t>(W, a.m_o - c0);
         const int64_t body = cnt & ~int64_t(3);
-        float* dst = pot + (size_t)s * W;
+        float* dst = pot + (size_t)sb * W;
         // the last few floats when the block is not a multiple of 16 bytes
         for (int64_t q = body; q < cnt; ++q) dst[q] = a.other[c0 + q];
-        mbar_arrive_tx(pot_full(s), (uint32_t)(body * 4));
-        if (body > 0) bulk_g2s(smem_u32(dst), a.other + c0, (uint32_t)(body * 4), pot_full(s));
+        mbar_arrive_tx(pot_full(sb), (uint32_t)(body * 4));
+        if (body > 0) bulk_g2s(smem_u32(dst), a.other + c0, (uint32_t)(body * 4), pot_full(sb));
         ++nb;
-        const int64_t e0 = a.tstart[pb + b], e1 = a.tstart[pb + b + 1];
+        if (++sb == kStages) { sb = 0; ub ^= 1u; }
         for (int64_t c = e0; c < e1; c += E) {
-          const int s2 = (int)(nc & 1);
-          if (nc >= 2 && !(ok = mbar_wait(ent_empty(s2), (uint32_t)(((nc >> 1) - 1) & 1),
-                                          abort_w, a.err, 2)))
-            break;
+          if (nc >= kStages && !(ok = mbar_wait(ent_empty(sc), uc ^ 1u, abort_w, a.err, 2))) break;
           const uint32_t len = (uint32_t)std::min<int64_t>(E, e1 - c);
-          mbar_arrive_tx(ent_full(s2), len * 8u);
-          bulk_g2s(smem_u32(emeta + (size_t)s2 * E), a.meta + c, len * 4u, ent_full(s2));
-          bulk_g2s(smem_u32(elam + (size_t)s2 * E), a.lam + c, len * 4u, ent_full(s2));
+          mbar_arrive_tx(ent_full(sc), len * 8u);
+          bulk_g2s(smem_u32(emeta + (size_t)sc * E), a.meta + c, len * 4u, ent_full(sc));
+          bulk_g2s(smem_u32(elam + (size_t)sc * E), a.lam + c, len * 4u, ent_full(sc));
           ++nc;
+          if (++sc == kStages) { sc = 0; uc ^= 1u; }
         }
+        e0 = e1;
       }
     }
     if (!ok) {
       // wait (bounded) for the copies in flight so none lands after the CTA leaves
-      for (long long k = std::max(0ll, nb - 2); k < nb; ++k) {
+      for (long long k = std::max(0ll, nb - kStages); k < nb; ++k) {
         const long long t0 = clock64();
-        while (!mbar_try(pot_full((int)(k & 1)), (uint32_t)((k >> 1) & 1)) &&
+        while (!mbar_try(pot_full((int)(k % kStages)), (uint32_t)((k / kStages) & 1)) &&
                clock64() - t0 < kWaitCycles) {
         }
       }
-      for (long long k = std::max(0ll, nc - 2); k < nc; ++k) {
+      for (long long k = std::max(0ll, nc - kStages); k < nc; ++k) {
         const long long t0 = clock64();
-        while (!mbar_try(ent_full((int)(k & 1)), (uint32_t)((k >> 1) & 1)) &&
+        while (!mbar_try(ent_full((int)(k % kStages)), (uint32_t)((k / kStages) & 1)) &&
                clock64() - t0 < kWaitCycles) {
         }
       }
@@ -491,7 +518,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   // terms above 2^k would overflow the high-part sum of the longest row
   const float capd = (longest <= 4096 && k >= 1) ? ((float)k - 0.01f) * 0.69314718f : -INFINITY;
   uint32_t chk_bits = 0;
-  long long nb = 0, nc = 0;
+  int sb = 0, sc = 0;       // stage of each ring
+  uint32_t ub = 0, uc = 0;  // parity of the current use of that stage
   bool ok = true;
   // Control flow that crosses a consumer barrier follows the shared abort word
   // (identical for all consumers after bar.sync), never a thread-local flag.
@@ -506,17 +534,20 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       sig[r] = r < rows ? __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]) : 0.0f;
     }
     for (int r = tid; r < (a.R + 31) / 32; r += kConsumers) flags[r] = 0u;
+    int64_t e0 = a.tstart[pb], e1n = a.tstart[pb + 1];
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     for (int b = 0; ok && b < a.B; ++b) {
-      const int s = (int)(nb & 1);
-      if (!(ok = warp_wait(pot_full(s), (uint32_t)((nb >> 1) & 1), abort_w, a.err, 3))) break;
-      ++nb;
+      const int64_t e1 = e1n;
+      // next tile's end: loaded now, used after this tile's waits
+      if (b + 1 < a.B) e1n = a.tstart[pb + b + 2];
+      const int s = sb;
+      if (!(ok = warp_wait(pot_full(s), ub, abort_w, a.err, 3))) break;
+      if (++sb == kStages) { sb = 0; ub ^= 1u; }
       const float* cur = pot + (size_t)s * W;
-      const int64_t e0 = a.tstart[pb + b], e1 = a.tstart[pb + b + 1];
       for (int64_t c = e0; c < e1; c += E) {
-        const int s2 = (int)(nc & 1);
-        if (!(ok = warp_wait(ent_full(s2), (uint32_t)((nc >> 1) & 1), abort_w, a.err, 4))) break;
-        ++nc;
+        const int s2 = sc;
+        if (!(ok = warp_wait(ent_full(s2), uc, abort_w, a.err, 4))) break;
+        if (++sc == kStages) { sc = 0; uc ^= 1u; }
         const int len = (int)std::min<int64_t>(E, e1 - c);
         const uint32_t* mt = emeta + (size_t)s2 * E;
         const float* lv = elam + (size_t)s2 * E;
@@ -543,6 +574,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(pot_empty(s));
+      e0 = e1;
     }
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     if (*abort_w) break;
