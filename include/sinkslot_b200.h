@@ -9,7 +9,8 @@
  *     that stream, exactly where the reference reads a value back with
  *     .item()/int()/bool().
  *   - No call allocates device memory.  Scratch comes from a caller-provided
- *     workspace whose size the matching *_workspace_bytes call reports.
+ *     workspace whose size the matching *_workspace_bytes call reports
+ *     (sinkslot_solve_csr_static alone uses the library's static array).
  *   - Return value: 0 on success, otherwise a status code (1 invalid argument,
  *     2 CUDA error, 3 workspace too small, 4 unsupported); the message is in
  *     sinkslot_last_error() (per calling thread).
@@ -164,6 +165,27 @@ int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                        const void* c_tiles, int64_t c_tiles_bytes, float* phi, float* psi,
                        float* work, int64_t work_floats, int64_t* iters_host, int* converged_host,
                        double* final_viol_host, void* stream);
+
+/* Capacity, in floats, of the library's static solve scratch (4 MiB held on
+ * every device that loads the library, until the process exits). */
+#define SINKSLOT_STATIC_SOLVE_FLOATS (1 << 20)
+
+/* sinkslot_solve_csr without the work buffer: the loop's scratch is the
+ * library's static device array (no counterpart in the reference; for callers
+ * that cannot allocate device scratch).  Allocates nothing.  Status 1 when
+ * sinkslot_solve_work_floats(n, m) > SINKSLOT_STATIC_SOLVE_FLOATS.  The first
+ * call on a device resolves the array's address and should come before any
+ * stream capture there; calls that overlap on one device share the array and
+ * race. */
+int sinkslot_solve_csr_static(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
+                              const float* r_lam, const int32_t* c_ptr, const void* c_idx,
+                              int c_idx_bytes, const float* c_lam, int64_t nnz,
+                              const float* log_a, const float* log_b, int64_t n, int64_t m,
+                              int variant, int stop_mode, int64_t n_iters, int64_t max_iter,
+                              int64_t check_every, double tol, double eps, double alpha,
+                              const void* r_tiles, int64_t r_tiles_bytes, const void* c_tiles,
+                              int64_t c_tiles_bytes, float* phi, float* psi, int64_t* iters_host,
+                              int* converged_host, double* final_viol_host, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Plan export and gradient

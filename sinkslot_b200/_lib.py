@@ -49,6 +49,10 @@ _SIGNATURES = {
                            c_i64, c_i64, c_int, c_int, c_i64, c_i64, c_i64, c_dbl, c_dbl, c_dbl,
                            c_vp, c_i64, c_vp, c_i64,
                            c_vp, c_vp, c_vp, c_i64, P_i64, P_int, P_dbl, c_vp],
+    "sinkslot_solve_csr_static": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_vp,
+                                  c_vp, c_i64, c_i64, c_int, c_int, c_i64, c_i64, c_i64, c_dbl,
+                                  c_dbl, c_dbl, c_vp, c_i64, c_vp, c_i64,
+                                  c_vp, c_vp, P_i64, P_int, P_dbl, c_vp],
     "sinkslot_tiles_bytes": [c_i64, c_i64, c_i64, P_i64, P_i64],
     "sinkslot_tiles_geometry": [c_i64, c_i64, c_i64, P_int],
     "sinkslot_build_tiles": [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp,
