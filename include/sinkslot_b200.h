@@ -132,10 +132,11 @@ int sinkslot_tiles_bytes(int64_t nseg, int64_t m_other, int64_t nnz, int64_t* la
 
 /* The tiled layout's geometry: geom_host[0..4] = panels P, rows per panel R,
  * column blocks B, log2 of the block width W, dynamic shared memory bytes.
- * Layout bytes: int64 header[8] | int64 tile_start[P*B + 1] | uint32 meta[nnz]
- * (row within panel << 16 | column within block) | float lam[nnz], each part
- * 256-byte aligned; tile t = p*B + b holds entries [tile_start[t],
- * tile_start[t+1]) in CSR order. */
+ * Layout bytes: int64 header[8] | int64 tile_start[P*B + 1] | uint32
+ * entries[cap][2] = {row within panel << 16 | column within block, lam bits},
+ * each part 256-byte aligned; tile t = p*B + b holds entries [tile_start[t],
+ * tile_start[t+1]) in CSR order, padded to a multiple of 32 with entries
+ * {R << 16, -inf}; cap = nnz + 31*P*B. */
 int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geom_host);
 
 /* Column-blocked layout of a CSR side for the shared-memory-staged half-step

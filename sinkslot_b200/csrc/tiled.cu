@@ -9,18 +9,24 @@
 // shared-memory load.
 //
 // Layout (built once per solve from the CSR side): tile (p, b) = the entries of
-// panel p whose column lies in block b, in CSR order, padded to a multiple of 4
-// entries (padding meta = 0xFFFFFFFF); per entry one uint32 (row within the
-// panel << 16 | column within the block) and the fp32 lam.
+// panel p whose column lies in block b, in CSR order, padded to a multiple of 32
+// entries (one warp slab); per entry one uint2 {row within the panel << 16 |
+// column within the block, fp32 lam bits}.  Padding names row R (a dummy row
+// of the panel state) with lam = -inf, so it adds an exact zero and the inner
+// loop needs no test for it.
 //
 // Pipeline (one CTA per SM, warp-specialised): one producer warp issues TMA
-// bulk copies (cp.async.bulk) of potential blocks and of tile entry chunks into
-// shared-memory rings of kStages stages, each stage guarded by a full/empty mbarrier
-// pair; 31 consumer warps wait on "full", read entries and potentials from
-// shared memory, accumulate, and arrive on "empty".  No CTA-wide barrier per
-// tile.  Every mbarrier wait is bounded by a clock budget: on timeout the kernel
-// records an error code, the producer waits (bounded) for the copies it issued,
-// and all warps leave.
+// bulk copies (cp.async.bulk) of potential blocks into a shared-memory ring of
+// kStages stages, each guarded by a full/empty mbarrier pair, and prefetches
+// each tile's entries into L2 (cp.async.bulk.prefetch) when it issues the
+// tile's block.  31 consumer warps read their slabs of entries straight from
+// L2 with coalesced 8-byte loads (the next tile's first slabs are in flight
+// while the current tile is processed), wait on "full", gather potentials from
+// shared memory, accumulate, and arrive on "empty".  Entries never pass through
+// shared memory, whose bandwidth the gathers and the row-state atomics need.
+// No CTA-wide barrier per tile.  Every mbarrier wait is bounded by a clock
+// budget: on timeout the kernel records an error code, the producer waits
+// (bounded) for the copies it issued, and all warps leave.
 //
 // Arithmetic: the log-sum-exp of a row is stabilised by the row's previous
 // value, sigma = base - self_old (the LSE the previous half-step produced), so
@@ -46,41 +52,48 @@
 
 namespace sinkslot {
 
-constexpr int kConsumerWarps = 31;  // + 1 producer warp = 1024 threads
+#ifndef SINKSLOT_TILE_WARPS
+#define SINKSLOT_TILE_WARPS 31
+#endif
+constexpr int kConsumerWarps = SINKSLOT_TILE_WARPS;  // + 1 producer warp
 constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kPipeThreads = kConsumers + 32;  // + one producer warp
-constexpr int kEntryUnroll = 8;
 constexpr size_t kSmemCap = 227 * 1024;
 
 // Build-time tuning of the pipeline (defaults measured on B200):
-//   SINKSLOT_TILE_STAGES   ring depth of both the potential and the entry ring
+//   SINKSLOT_TILE_STAGES   depth of the potential-block ring
 //   SINKSLOT_TILE_ROWS_KB  budget for the per-row state; more panels than SMs
 //                          are used (each SM walks several) to stay within it
 //   SINKSLOT_TILE_MAX_LOGW widest potential block (2^x floats)
 #ifndef SINKSLOT_TILE_STAGES
-#define SINKSLOT_TILE_STAGES 3
+#define SINKSLOT_TILE_STAGES 2
 #endif
 #ifndef SINKSLOT_TILE_ROWS_KB
-#define SINKSLOT_TILE_ROWS_KB 48
+#define SINKSLOT_TILE_ROWS_KB 96
 #endif
 #ifndef SINKSLOT_TILE_MAX_LOGW
 #define SINKSLOT_TILE_MAX_LOGW 14
 #endif
 constexpr int kStages = SINKSLOT_TILE_STAGES;
-constexpr size_t kBarBytes = align_up(32 * kStages + 16, 128);  // 4 mbarriers per stage + abort
+constexpr size_t kBarBytes = align_up(16 * kStages + 16, 128);  // 2 mbarriers per stage + abort
 constexpr float kFixScale = 4294967296.0f;  // 2^32
 constexpr double kFixInv = 1.0 / 4294967296.0;
 constexpr unsigned long long kFixMin = 1ull << 24;  // sums below 2^-8 go to the exact pass
 constexpr int kLoBits = 20;
 constexpr long long kWaitCycles = 8000000000ll;  // ~4 s at 2 GHz: a wait this long is a bug
 
-// shared memory per panel row: sigma, high sum, low sum (4 B each) + a flag bit
-static size_t rows_smem(int R) {
-  return 3 * align_up((size_t)R * 4, 16) + align_up((size_t)((R + 31) / 32) * 4, 16);
+constexpr int kSlab = 32;  // tiles are padded to whole warp slabs of entries
+
+// Shared memory of the per-row state: rows 0..R-1 of the panel and a dummy row R
+// (the target of tile padding), 12 bytes each at offset 12 r: sigma (float),
+// high sum, low sum (uint32); then one flag bit per row.
+__host__ __device__ inline size_t rows_flags_off(int R) { return align_up((size_t)(R + 1) * 12, 16); }
+__host__ __device__ inline size_t rows_smem(int R) {
+  return align_up(rows_flags_off(R) + (size_t)((R + 1 + 31) / 32) * 4, 128);
 }
 
-static size_t pipe_smem(int R, int W, int E) {
-  return (size_t)kStages * ((size_t)W * 4 + (size_t)E * 8) + rows_smem(R) + kBarBytes;
+static size_t pipe_smem(int R, int W) {
+  return rows_smem(R) + (size_t)kStages * (size_t)W * 4 + kBarBytes;
 }
 
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
@@ -96,43 +109,25 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   // for the smallest rings
   const size_t rows_budget = (size_t)SINKSLOT_TILE_ROWS_KB * 1024;
   while ((rows_smem((int)std::min<int64_t>(R, 1 << 20)) > rows_budget && R > 32) || R > 65535 ||
-         pipe_smem((int)std::min<int64_t>(R, 1 << 20), 256, 256) > kSmemCap) {
+         pipe_smem((int)std::min<int64_t>(R, 1 << 20), 256) > kSmemCap) {
     P += sms;
     R = ceil_div64(nseg, P);
   }
-  // widest block first (fewer tiles); the entry chunk sized to hold a typical
-  // tile (256..4096 entries), shrunk if the rings do not fit
-  const int logW_need = [&] {
-    int l = 2;
-    while (l < SINKSLOT_TILE_MAX_LOGW && ((int64_t)1 << l) < m_o) ++l;
-    return l;
-  }();
-  int logW = 2, E = 256;
-  for (int lw = logW_need; lw >= 2; --lw) {
-    const int64_t B = ceil_div64(m_o, (int64_t)1 << lw);
-    int64_t want = ceil_div64(std::max<int64_t>(nnz, 1), P * B);
-    want = std::min<int64_t>(4096, std::max<int64_t>(256, (want + 255) / 256 * 256));
-    int e = (int)want;
-    while (e > 256 && pipe_smem((int)R, 1 << lw, e) > kSmemCap) e -= 256;
-    if (pipe_smem((int)R, 1 << lw, e) <= kSmemCap) {
-      logW = lw;
-      E = e;
-      break;
-    }
-  }
+  // the widest block (fewest tiles) whose ring fits
+  int logW = 2;
+  while (logW < SINKSLOT_TILE_MAX_LOGW && ((int64_t)1 << logW) < m_o) ++logW;
+  while (logW > 8 && pipe_smem((int)R, 1 << logW) > kSmemCap) --logW;
   g.P = (int)P;
   g.R = (int)R;
   g.logW = logW;
-  g.E = E;
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
-  g.smem_bytes = pipe_smem((int)R, 1 << logW, E);
+  g.smem_bytes = pipe_smem((int)R, 1 << logW);
   const int64_t ntiles = (int64_t)g.P * g.B;
-  g.cap = nnz + 3 * ntiles;
+  g.cap = nnz + (kSlab - 1) * ntiles;
   Carver cv(nullptr, 0);
   cv.take<int64_t>(8);            // header: [0] longest row
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
-  cv.take<uint32_t>(std::max<int64_t>(g.cap, 1));  // meta
-  cv.take<float>(std::max<int64_t>(g.cap, 1));     // lam
+  cv.take<uint2>(std::max<int64_t>(g.cap, 1));  // entries {meta, lam bits}
   g.layout_bytes = cv.used;
   Carver bw(nullptr, 0);
   const int64_t e = std::max<int64_t>(nnz, 1);
@@ -149,8 +144,7 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
 struct LayoutPtrs {
   int64_t* header;
   int64_t* tstart;
-  uint32_t* meta;
-  float* lam;
+  uint2* ent;
 };
 
 static LayoutPtrs carve_layout(void* layout, const TileGeom& g) {
@@ -158,8 +152,7 @@ static LayoutPtrs carve_layout(void* layout, const TileGeom& g) {
   LayoutPtrs p;
   p.header = cv.take<int64_t>(8);
   p.tstart = cv.take<int64_t>((int64_t)g.P * g.B + 1);
-  p.meta = cv.take<uint32_t>(std::max<int64_t>(g.cap, 1));
-  p.lam = cv.take<float>(std::max<int64_t>(g.cap, 1));
+  p.ent = cv.take<uint2>(std::max<int64_t>(g.cap, 1));
   return p;
 }
 
@@ -199,9 +192,9 @@ __global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __r
   }
 }
 
-// ustart[t] = #{sorted keys < t}; cnt4[t] = entries of tile t rounded up to 4
+// ustart[t] = #{sorted keys < t}; cntp[t] = entries of tile t rounded up to a slab
 __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
-                                   int64_t* __restrict__ ustart, int64_t* __restrict__ cnt4) {
+                                   int64_t* __restrict__ ustart, int64_t* __restrict__ cntp) {
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t <= ntiles;
        t += (int64_t)gridDim.x * blockDim.x) {
     auto lb = [&](int64_t v) {
@@ -214,17 +207,16 @@ __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nn
     };
     const int64_t s = lb(t);
     ustart[t] = s;
-    if (t < ntiles) cnt4[t] = (lb(t + 1) - s + 3) & ~int64_t(3);
+    if (t < ntiles) cntp[t] = (lb(t + 1) - s + kSlab - 1) & ~int64_t(kSlab - 1);
   }
 }
 
-__global__ void fill_meta_kernel(uint32_t* __restrict__ meta, float* __restrict__ lam,
-                                 int64_t cap) {
+// padding entries: the dummy row R, column 0, lam = -inf (a zero term)
+__global__ void fill_pad_kernel(uint2* __restrict__ ent, int64_t cap, int R) {
+  const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < cap;
-       q += (int64_t)gridDim.x * blockDim.x) {
-    meta[q] = 0xFFFFFFFFu;
-    lam[q] = 0.0f;
-  }
+       q += (int64_t)gridDim.x * blockDim.x)
+    ent[q] = pad;
 }
 
 template <typename IT>
@@ -234,7 +226,7 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ perm,
                                     const float* __restrict__ lam, int64_t nnz, int R, int logW,
                                     const int64_t* __restrict__ ustart,
                                     const int64_t* __restrict__ tstart,
-                                    uint32_t* __restrict__ meta, float* __restrict__ tlam) {
+                                    uint2* __restrict__ ent) {
   const uint32_t wmask = (1u << logW) - 1u;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
        q += (int64_t)gridDim.x * blockDim.x) {
@@ -243,8 +235,7 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ perm,
     const int64_t pos = tstart[t] + (q - ustart[t]);
     const uint32_t r = rowid[k];
     const uint32_t c = (uint32_t)idx[k];
-    meta[pos] = ((r % (uint32_t)R) << 16) | (c & wmask);
-    tlam[pos] = lam[k];
+    ent[pos] = make_uint2(((r % (uint32_t)R) << 16) | (c & wmask), __float_as_uint(lam[k]));
   }
 }
 
@@ -272,7 +263,7 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
     return kWorkspaceTooSmall;
   }
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.header, 0, 8 * sizeof(int64_t), st));
-  fill_meta_kernel<<<grid_t(g.cap, 256), 256, 0, st>>>(L.meta, L.lam, g.cap);
+  fill_pad_kernel<<<grid_t(g.cap, 256), 256, 0, st>>>(L.ent, g.cap, g.R);
   SINKSLOT_CHECK_LAUNCH();
   rowid_kernel<<<grid_t(g.nseg, 256), 256, 0, st>>>(
       ptr, g.nseg, rowid, reinterpret_cast<unsigned long long*>(L.header));
@@ -302,11 +293,11 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   if (idx_bytes == 2)
     tile_scatter_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
         perm, skey, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
-        L.tstart, L.meta, L.lam);
+        L.tstart, L.ent);
   else
     tile_scatter_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
         perm, skey, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
-        L.tstart, L.meta, L.lam);
+        L.tstart, L.ent);
   SINKSLOT_CHECK_LAUNCH();
   return kOk;
 }
@@ -337,6 +328,20 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same test, but a thread whose phase is not complete is suspended (woken
+// when it completes, or after at most kSuspendNs) instead of returning at once:
+// waiting warps then take no issue slots from the working ones.
+constexpr uint32_t kSuspendNs = 200000;
+__device__ __forceinline__ bool mbar_try_suspend(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // 1-D bulk copy global -> shared, completion counted on `bar` (16-B aligned, size % 16 == 0)
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
                                          uint32_t bar) {
@@ -354,7 +359,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int* err, int code) {
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_suspend(bar, parity)) return true;
     if (*abort_w) return false;
     if (clock64() - t0 > kWaitCycles) {
       atomicCAS(err, 0, code);
@@ -372,7 +377,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
                                           int* err, int code) {
   const long long t0 = clock64();
   while (true) {
-    const bool done = mbar_try(bar, parity);
+    const bool done = mbar_try_suspend(bar, parity);
     if (__all_sync(0xffffffffu, done)) return true;
     int stop = 0;
     if ((threadIdx.x & 31) == 0) {
@@ -393,11 +398,10 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 // ---------------------------------------------------------------------------
 struct TKArgs {
   int64_t nseg, m_o;
-  int P, R, B, logW, E;
+  int P, R, B, logW;
   const int64_t* header;
   const int64_t* tstart;
-  const uint32_t* meta;
-  const float* lam;
+  const uint2* ent;
   const float* other;
   const float* base;
   const float* self_old;
@@ -411,30 +415,106 @@ struct TKArgs {
   int* err;
 };
 
+// State of panel row r: {sigma bits, high sum, low sum} at byte 12 r of the
+// dynamic shared memory (a fixed base, so the address is one multiply).
+__device__ __forceinline__ uint32_t* row_state(unsigned char* smem, uint32_t r) {
+  return reinterpret_cast<uint32_t*>(smem + r * 12u);
+}
+
+// One entry {row << 16 | column, lam bits}: the exponent d = lam + cur[column]
+// - sigma of its term, and the state of its row.  Padding entries name the
+// dummy row with lam = -inf, so d = -inf and the term is an exact zero.
+__device__ __forceinline__ float entry_exponent(unsigned char* smem, const float* cur, uint2 e,
+                                                uint32_t*& st) {
+  st = row_state(smem, e.x >> 16);
+  return __fsub_rn(__fadd_rn(__uint_as_float(e.y), cur[e.x & 0xFFFFu]), __uint_as_float(st[0]));
+}
+
+// 2^x (hardware approximation; results below 2^-126 flush to zero, far below
+// the 2^-32 resolution of the sums)
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// exp(d) in 2^-32 fixed point, added to the row's high and low partial sums.
+// Called for every entry; when d exceeds the cap (or is NaN) the caller has
+// flagged the row for the exact pass and its sums are unused.
+__device__ __forceinline__ void accumulate(uint32_t* st, float d) {
+  const unsigned long long q = __float2ull_rn(exp2_approx(d * 1.44269504088896341f) * kFixScale);
+  atomicAdd(st + 1, (uint32_t)(q >> kLoBits));
+  atomicAdd(st + 2, (uint32_t)q & ((1u << kLoBits) - 1u));
+}
+
+__device__ __forceinline__ void flag_row(uint32_t* flags, uint2 e) {
+  const uint32_t r = e.x >> 16;
+  atomicOr(flags + (r >> 5), 1u << (r & 31));
+}
+
+// Prefetch of a byte range into L2 (16-byte aligned start, size a multiple of 16).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Lane `lane` of slabs g .. g+3 of the tile whose entries start at e0 (only the
+// slabs below nsl are loaded): coalesced 8-byte streaming loads, 256 bytes per
+// slab.
+__device__ __forceinline__ void load_group(const uint2* ent, int64_t e0, int nsl, int g, int lane,
+                                           uint2 (&e)[4]) {
+  const uint2* p = ent + e0 + (int64_t)g * kSlab + lane;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (g + j < nsl) e[j] = ld_stream(p + j * kSlab);
+}
+
+// The terms of a group of `cnt` (>= 1) slabs; when all four exist one vote per
+// group checks the cap of its 128 terms.
+__device__ __forceinline__ void process_group(unsigned char* smem, uint32_t* flags,
+                                              const float* cur, const uint2 (&e)[4], int cnt,
+                                              float capd) {
+  if (cnt >= 4) {
+    uint32_t* st[4];
+    float d[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) d[j] = entry_exponent(smem, cur, e[j], st[j]);
+    const bool in_cap = (d[0] <= capd) & (d[1] <= capd) & (d[2] <= capd) & (d[3] <= capd);
+    if (!__all_sync(0xffffffffu, in_cap)) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (!(d[j] <= capd)) flag_row(flags, e[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) accumulate(st[j], d[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      if (j < cnt) {
+        uint32_t* st;
+        const float d = entry_exponent(smem, cur, e[j], st);
+        if (!(d <= capd)) flag_row(flags, e[j]);
+        accumulate(st, d);
+      }
+    }
+  }
+}
+
 template <int OUT, int CHK>
 __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const TKArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int W = 1 << a.logW;
-  const int E = a.E;
-  const size_t rbytes = align_up((size_t)a.R * 4, 16);
-  // [kStages][W] potential blocks, [kStages][E] entry metas, [kStages][E] entry lams
-  float* pot = reinterpret_cast<float*>(smem);
-  uint32_t* emeta = reinterpret_cast<uint32_t*>(smem + (size_t)kStages * W * 4);
-  float* elam = reinterpret_cast<float*>(smem + (size_t)kStages * W * 4 + (size_t)kStages * E * 4);
-  unsigned char* rowp = smem + (size_t)kStages * ((size_t)W * 4 + (size_t)E * 8);
-  float* sig = reinterpret_cast<float*>(rowp);
-  uint32_t* hi = reinterpret_cast<uint32_t*>(rowp + rbytes);
-  uint32_t* lo = reinterpret_cast<uint32_t*>(rowp + 2 * rbytes);
-  uint32_t* flags = reinterpret_cast<uint32_t*>(rowp + 3 * rbytes);
+  // row state at offset 0 (12 bytes per row: sigma, high sum, low sum; row R is
+  // the padding target), flag bits, then [kStages][W] potential blocks, the
+  // mbarriers and the abort word
+  uint32_t* flags = reinterpret_cast<uint32_t*>(smem + rows_flags_off(a.R));
+  float* pot = reinterpret_cast<float*>(smem + rows_smem(a.R));
   unsigned long long* bars = reinterpret_cast<unsigned long long*>(
-      rowp + 3 * rbytes + align_up((size_t)((a.R + 31) / 32) * 4, 16));
-  volatile int* abort_w = reinterpret_cast<volatile int*>(bars + 4 * kStages);
-  // bars, kStages each: potential full, potential empty, entries full, entries empty
+      smem + rows_smem(a.R) + (size_t)kStages * W * 4);
+  volatile int* abort_w = reinterpret_cast<volatile int*>(bars + 2 * kStages);
+  // bars, kStages each: potential block full, potential block empty
   const uint32_t bar0 = smem_u32(bars);
   auto pot_full = [&](int s) { return bar0 + 8u * (uint32_t)s; };
   auto pot_empty = [&](int s) { return bar0 + 8u * (uint32_t)(kStages + s); };
-  auto ent_full = [&](int s) { return bar0 + 8u * (uint32_t)(2 * kStages + s); };
-  auto ent_empty = [&](int s) { return bar0 + 8u * (uint32_t)(3 * kStages + s); };
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -444,8 +524,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     for (int s = 0; s < kStages; ++s) {
       mbar_init(pot_full(s), 1);
       mbar_init(pot_empty(s), kConsumerWarps);
-      mbar_init(ent_full(s), 1);
-      mbar_init(ent_empty(s), kConsumerWarps);
     }
     *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -456,10 +534,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   if (warp == kConsumerWarps) {
     // ---------------- producer warp: lane 0 issues every copy ----------------
     if (lane != 0) return;
-    // blocks / chunks issued so far; stage = count % kStages, use = count / kStages
-    long long nb = 0, nc = 0;
-    int sb = 0, sc = 0;          // current stage of each ring
-    uint32_t ub = 0, uc = 0;     // parity of the current use of that stage
+    long long nb = 0;  // blocks issued so far: stage nb % kStages, use nb / kStages
+    int sb = 0;
+    uint32_t ub = 0;   // parity of the current use of stage sb
     bool ok = true;
     for (int p = blockIdx.x; ok && p < a.P; p += gridDim.x) {
       if ((int64_t)p * a.R >= a.nseg) break;
@@ -469,6 +546,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
         const int64_t e1 = e1n;
         // next tile's end: loaded now, used after this tile's waits
         if (b + 1 < a.B) e1n = a.tstart[pb + b + 2];
+        // the tile's entries into L2 ahead of the consumers' loads
+        if (e1 > e0) prefetch_l2(a.ent + e0, (uint32_t)((e1 - e0) * sizeof(uint2)));
         if (nb >= kStages && !(ok = mbar_wait(pot_empty(sb), ub ^ 1u, abort_w, a.err, 1))) break;
         const int64_t c0 = (int64_t)b * W;
         const int64_t cnt = std::min<int64_t>(W, a.m_o - c0);
@@ -480,15 +559,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
         if (body > 0) bulk_g2s(smem_u32(dst), a.other + c0, (uint32_t)(body * 4), pot_full(sb));
         ++nb;
         if (++sb == kStages) { sb = 0; ub ^= 1u; }
-        for (int64_t c = e0; c < e1; c += E) {
-          if (nc >= kStages && !(ok = mbar_wait(ent_empty(sc), uc ^ 1u, abort_w, a.err, 2))) break;
-          const uint32_t len = (uint32_t)std::min<int64_t>(E, e1 - c);
-          mbar_arrive_tx(ent_full(sc), len * 8u);
-          bulk_g2s(smem_u32(emeta + (size_t)sc * E), a.meta + c, len * 4u, ent_full(sc));
-          bulk_g2s(smem_u32(elam + (size_t)sc * E), a.lam + c, len * 4u, ent_full(sc));
-          ++nc;
-          if (++sc == kStages) { sc = 0; uc ^= 1u; }
-        }
         e0 = e1;
       }
     }
@@ -497,12 +567,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       for (long long k = std::max(0ll, nb - kStages); k < nb; ++k) {
         const long long t0 = clock64();
         while (!mbar_try(pot_full((int)(k % kStages)), (uint32_t)((k / kStages) & 1)) &&
-               clock64() - t0 < kWaitCycles) {
-        }
-      }
-      for (long long k = std::max(0ll, nc - kStages); k < nc; ++k) {
-        const long long t0 = clock64();
-        while (!mbar_try(ent_full((int)(k % kStages)), (uint32_t)((k / kStages) & 1)) &&
                clock64() - t0 < kWaitCycles) {
         }
       }
@@ -518,8 +582,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   // terms above 2^k would overflow the high-part sum of the longest row
   const float capd = (longest <= 4096 && k >= 1) ? ((float)k - 0.01f) * 0.69314718f : -INFINITY;
   uint32_t chk_bits = 0;
-  int sb = 0, sc = 0;       // stage of each ring
-  uint32_t ub = 0, uc = 0;  // parity of the current use of that stage
+  int sb = 0;
+  uint32_t ub = 0;
   bool ok = true;
   // Control flow that crosses a consumer barrier follows the shared abort word
   // (identical for all consumers after bar.sync), never a thread-local flag.
@@ -528,66 +592,55 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     const int rows = (int)std::min<int64_t>(a.R, a.nseg - row0);
     if (rows <= 0) break;
     const int64_t pb = (int64_t)p * a.B;
-    for (int r = tid; r < a.R; r += kConsumers) {
-      hi[r] = 0u;
-      lo[r] = 0u;
-      sig[r] = r < rows ? __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]) : 0.0f;
+    for (int r = tid; r <= a.R; r += kConsumers) {
+      uint32_t* st = row_state(smem, (uint32_t)r);
+      st[0] = __float_as_uint(
+          r < rows ? __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]) : 0.0f);
+      st[1] = 0u;
+      st[2] = 0u;
     }
-    for (int r = tid; r < (a.R + 31) / 32; r += kConsumers) flags[r] = 0u;
-    int64_t e0 = a.tstart[pb], e1n = a.tstart[pb + 1];
+    for (int r = tid; r < (a.R + 1 + 31) / 32; r += kConsumers) flags[r] = 0u;
+    // Tile b holds slabs [e0, e1) / 32 of the layout.  Warp w takes groups of
+    // four consecutive slabs starting at 4w, 4w + 4*31, ...; its first group of
+    // the next tile is loaded while the current tile is processed.
+    int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
+    uint2 en[4];
+    load_group(a.ent, e0, (int)((e1 - e0) / kSlab), 4 * warp, lane, en);
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     for (int b = 0; ok && b < a.B; ++b) {
-      const int64_t e1 = e1n;
-      // next tile's end: loaded now, used after this tile's waits
-      if (b + 1 < a.B) e1n = a.tstart[pb + b + 2];
+      const int nsl = (int)((e1 - e0) / kSlab);
+      uint2 e[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) e[j] = en[j];
+      const int64_t f0 = e1;
+      const int64_t f1 = b + 1 < a.B ? a.tstart[pb + b + 2] : e1;
+      load_group(a.ent, f0, (int)((f1 - f0) / kSlab), 4 * warp, lane, en);
       const int s = sb;
       if (!(ok = warp_wait(pot_full(s), ub, abort_w, a.err, 3))) break;
       if (++sb == kStages) { sb = 0; ub ^= 1u; }
       const float* cur = pot + (size_t)s * W;
-      for (int64_t c = e0; c < e1; c += E) {
-        const int s2 = sc;
-        if (!(ok = warp_wait(ent_full(s2), uc, abort_w, a.err, 4))) break;
-        if (++sc == kStages) { sc = 0; uc ^= 1u; }
-        const int len = (int)std::min<int64_t>(E, e1 - c);
-        const uint32_t* mt = emeta + (size_t)s2 * E;
-        const float* lv = elam + (size_t)s2 * E;
-        for (int i0 = 0; i0 < len; i0 += kConsumers * kEntryUnroll) {
-#pragma unroll
-          for (int u = 0; u < kEntryUnroll; ++u) {
-            const int i = i0 + u * kConsumers + tid;
-            if (i >= len) break;
-            const uint32_t m = mt[i];
-            if (m == 0xFFFFFFFFu) continue;
-            const uint32_t r = m >> 16;
-            const float d = __fsub_rn(__fadd_rn(lv[i], cur[m & 0xFFFFu]), sig[r]);
-            if (!(d <= capd)) {
-              atomicOr(flags + (r >> 5), 1u << (r & 31));
-            } else {
-              const unsigned long long q = __float2ull_rn(__expf(d) * kFixScale);
-              atomicAdd(hi + r, (uint32_t)(q >> kLoBits));
-              atomicAdd(lo + r, (uint32_t)(q & ((1u << kLoBits) - 1u)));
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(ent_empty(s2));
+      for (int g = 4 * warp; g < nsl; g += 4 * kConsumerWarps) {
+        if (g != 4 * warp) load_group(a.ent, e0, nsl, g, lane, e);
+        process_group(smem, flags, cur, e, nsl - g, capd);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(pot_empty(s));
-      e0 = e1;
+      e0 = f0;
+      e1 = f1;
     }
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     if (*abort_w) break;
     for (int r = tid; r < rows; r += kConsumers) {
       const int64_t seg = row0 + r;
-      const unsigned long long q = ((unsigned long long)hi[r] << kLoBits) + lo[r];
+      const uint32_t* st = row_state(smem, (uint32_t)r);
+      const unsigned long long q = ((unsigned long long)st[1] << kLoBits) + st[2];
       const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
       if (flagged || q < kFixMin) {
         a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
         continue;
       }
       const float tot = (float)((double)q * kFixInv);
-      const float lse = __fadd_rn(sig[r], logf(tot));
+      const float lse = __fadd_rn(__uint_as_float(st[0]), logf(tot));
       segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
                                  chk_bits);
     }
@@ -629,11 +682,9 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.R = h.g.R;
   a.B = h.g.B;
   a.logW = h.g.logW;
-  a.E = h.g.E;
   a.header = L.header;
   a.tstart = L.tstart;
-  a.meta = L.meta;
-  a.lam = L.lam;
+  a.ent = L.ent;
   a.other = h.other;
   a.base = h.base;
   a.self_old = h.self_old;

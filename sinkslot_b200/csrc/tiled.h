@@ -10,10 +10,10 @@ namespace sinkslot {
 // Geometry of a tiled layout: P panels of R rows; the gathered axis (length
 // m_o) cut into B blocks of W = 2^logW entries.  Tile (p, b) holds the entries
 // of panel p whose column falls in block b, in CSR order, padded to a multiple
-// of 4 entries; the kernel streams a tile in chunks of at most E entries.
+// of 32 entries (warp slabs).
 struct TileGeom {
   int64_t nseg = 0, m_o = 0, nnz = 0;
-  int P = 0, R = 0, B = 0, logW = 0, E = 0;
+  int P = 0, R = 0, B = 0, logW = 0;
   int64_t cap = 0;          // entries in the layout (nnz plus tile padding)
   size_t smem_bytes = 0;    // dynamic shared memory of the tiled kernel
   size_t layout_bytes = 0;  // header + tile_start + meta + lam

@@ -69,13 +69,13 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     P, R, B, logW, smem = _geometry(n, m, nnz)
     assert smem <= 227 * 1024 and R < 65536 and P * R >= n and B << logW >= m
     T = P * B
-    cap = nnz + 3 * T
+    cap = nnz + 31 * T
     off = _align(64)
     tstart = layout[off:off + 8 * (T + 1)].view(np.int64)
     off = _align(off + 8 * (T + 1))
-    meta = layout[off:off + 4 * cap].view(np.uint32)
-    off = _align(off + 4 * cap)
-    tlam = layout[off:off + 4 * cap].view(np.float32)
+    ent = layout[off:off + 8 * cap].view(np.uint32).reshape(cap, 2)
+    meta = ent[:, 0]
+    tlam = ent[:, 1].copy().view(np.float32)
     ptr_h = ptr.cpu().numpy().astype(np.int64)
     idx_h = idx.cpu().numpy().astype(np.int64)
     lam_h = lam.cpu().numpy()
@@ -83,10 +83,11 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     tile_of = (row_of // R) * B + (idx_h >> logW)
     order = np.argsort(tile_of, kind="stable")
     counts = np.bincount(tile_of, minlength=T)
-    padded = (counts + 3) // 4 * 4
+    padded = (counts + 31) // 32 * 32
     np.testing.assert_array_equal(tstart, np.concatenate([[0], np.cumsum(padded)]))
-    want_meta = np.full(cap, 0xFFFFFFFF, dtype=np.uint64)
-    want_lam = np.zeros(cap, dtype=np.float32)
+    # padding: the dummy row R, column 0, lam = -inf
+    want_meta = np.full(cap, R << 16, dtype=np.uint64)
+    want_lam = np.full(cap, -np.inf, dtype=np.float32)
     ustart = np.concatenate([[0], np.cumsum(counts)])
     pos = tstart[tile_of[order]] + (np.arange(nnz) - ustart[tile_of[order]])
     want_meta[pos] = ((row_of[order] % R) << 16) | (idx_h[order] & ((1 << logW) - 1))
