@@ -9,9 +9,12 @@ configuration; the reference publishes no number for it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-One process per GPU; for N > 1 launch under torch.distributed.run.  N > 1 runs
-one independent problem per rank (batch sharding: no data-path collective,
-weak scaling); the value is all ranks' iterations over the slowest rank's time.
+One process per GPU; for N > 1 launch under torch.distributed.run.  N > 1
+solves one problem of N * 2^20 points per cloud whose rows and columns are
+partitioned over the ranks (2^20 of each per rank: weak scaling), the potential
+slices exchanged by peer stores after every half-step; the value counts
+iterations of 2^20-point problems (N per iteration) over the slowest rank's
+time.  ``--replicas`` instead runs one independent 2^20 problem per rank.
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 C port in oracle/, all host threads) on the same workload; rank 0 only.
 Rank 0 prints one JSON line.
@@ -60,8 +63,8 @@ def ncu_traffic():
         return None
 
 
-def make_inputs(rank: int):
-    w = WORKLOAD
+def make_inputs(rank: int, w=None):
+    w = WORKLOAD if w is None else w
     torch.manual_seed(w["data_seed"] + 1000 * rank)
     x = torch.randn(w["n"], w["d"])
     y = torch.randn(w["m"], w["d"]) + w["shift"]
@@ -176,6 +179,8 @@ def run_b200(args):
     from sinkslot_b200.solver import cost_and_lam, sot_plan_coo, to_csr
 
     world, rank, local = dist_setup(args.gpus)
+    if world > 1 and not args.replicas:
+        return run_b200_sharded(args, world, rank, local)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -325,6 +330,117 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_b200_sharded(args, world, rank, local):
+    """N > 1: one problem of N * 2^20 points per cloud, rows and columns
+    partitioned over the N ranks (2^20 of each per rank: weak scaling), the
+    potentials exchanged by peer stores after every half-step."""
+    import torch.distributed as dist
+    import sinkslot_b200
+    from sinkslot_b200.sharded import ShardedSolver, sinkslot_solve_sharded
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sinkslot_b200.load_library()
+    w = dict(WORKLOAD)
+    w["n"] *= world
+    w["m"] *= world
+    x, y, a, b = make_inputs(0, w)  # identical on every rank
+    X, Y, A, B = (t.to(dev) for t in (x, y, a, b))
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    solver = ShardedSolver(X, Y, A, B, w["eps"], L=w["L"], seed=w["proj_seed"])
+    torch.cuda.synchronize(dev)
+    setup_ms = (time.perf_counter() - t0) * 1e3
+    nnz = int(solver.rows.numel())
+    solver.solve(max(args.warmup, 0), copy_out=False)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    solver.solve(args.steps, copy_out=False)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world, dev)
+    # units: iterations of a 2^20-point problem (each iteration here is `world` of them)
+    value = world * args.steps / (ms / 1e3) if ms > 0 else 0.0
+    t_half = ms / 1e3 / (2 * args.steps)
+    # this rank's bytes per half-step: its slice's entries and segments
+    r_nnz, c_nnz = solver.row[3], solver.col[3]
+    bytes_row = r_nnz * (solver.row[1].element_size() + 4) + 16 * solver.nr
+    bytes_col = c_nnz * (solver.col[1].element_size() + 4) + 16 * solver.nc
+    achieved = max_over_ranks(-((bytes_row + bytes_col) / (2 * t_half) / 1e9), world, dev)
+    achieved = -achieved  # the slowest rank's rate
+    solver.close()
+    del solver
+    peak, peak_kind = measured_peak_gbs()
+
+    # end to end through the public API from pinned host buffers (support build,
+    # the partitioned solve, potentials back)
+    xh, yh, ah, bh = (t.pin_memory() for t in (x, y, a, b))
+    phi_h = torch.empty(w["n"]).pin_memory()
+    psi_h = torch.empty(w["m"]).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    q0.record(stream)
+    r = sinkslot_solve_sharded(xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True),
+                               ah.to(dev, non_blocking=True), bh.to(dev, non_blocking=True),
+                               w["eps"], w["L"], w["proj_seed"], w["n_iters"])
+    phi_h.copy_(r.phi, non_blocking=True)
+    psi_h.copy_(r.psi, non_blocking=True)
+    q1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(q0.elapsed_time(q1), world, dev)
+    e2e_value = world * w["n_iters"] / (e2e_ms / 1e3)
+    h2d = sum(t.numel() * t.element_size() for t in (x, y, a, b))
+    d2h = (w["n"] + w["m"]) * 4
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD_NAME.replace(
+                           "N=M=2^20", f"N=M={world}x2^20 partitioned over {world} GPUs"),
+                       "n": w["n"], "m": w["m"], "d": w["d"], "L": w["L"], "eps": w["eps"],
+                       "nnz": nnz,
+                       "parallelism": f"rows and columns partitioned over {world} GPUs; "
+                                      f"potential slices exchanged by peer stores after every "
+                                      f"half-step",
+                       "unit_note": f"one step = one iteration of the {world}x2^20 problem = "
+                                    f"{world} iterations of the 2^20 problem",
+                       "l2": "inputs larger than L2: %.2f GB of CSR+CSC streamed per rank "
+                             "per iteration" % ((bytes_row + bytes_col) / 1e9),
+                       "setup_ms": round(setup_ms, 1)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": peak_kind, "traffic": None,
+                         "kernel": "per rank: tiled_half_step_kernel + exact pass + peer push "
+                                   "+ epoch wait, per half-step, averaged over the timed region",
+                         "bytes_per_half_step_rank0": {"row": bytes_row, "col": bytes_col},
+                         "half_step_us": round(t_half * 1e6, 2)},
+            "cpu_baseline": None,
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "step": "sinkslot_solve_sharded(...) from pinned host x, y, a, b: support "
+                            "build + %d iterations + potentials back" % w["n_iters"]},
+            # first iteration: exact + push + wait per side; later: tiled + exact + push + wait
+            "gpu_launches": 6 + 8 * (args.steps - 1),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def cpu_baseline_from_support(rows, cols, lam, log_a, log_b, w, budget_s: float = 15.0):
     """The oracle's torch-backend iteration (C, OpenMP, all host threads) on the
     same support, a bounded number of iterations."""
@@ -405,6 +521,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--plain", action="store_true",
                     help="time the exact half-step kernel alone (no shared-memory tiles)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: one independent 2^20 problem per GPU instead of one "
+                         "partitioned problem")
     ap.add_argument("--log2n", type=int, default=20,
                     help="points per cloud = 2^log2n (20: the headline problem; smaller sizes "
                          "are for profiling captures)")

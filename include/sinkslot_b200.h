@@ -189,6 +189,54 @@ int sinkslot_solve_csr_static(const int32_t* r_ptr, const void* r_idx, int r_idx
                               int* converged_host, double* final_viol_host, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Row/column-partitioned solve over the GPUs of one node (one process each)
+ * ------------------------------------------------------------------------- */
+
+#define SINKSLOT_IPC_HANDLE_BYTES 64
+
+/* CUDA IPC handle of the allocation holding `ptr` (64 bytes into handle_host)
+ * and ptr's byte offset inside it, for a peer process to map with
+ * sinkslot_ipc_import (no counterpart in the reference). */
+int sinkslot_ipc_export(const void* ptr, void* handle_host, int64_t* offset_host);
+/* Maps a peer's allocation (peer access enabled); *ptr_host = base + offset. */
+int sinkslot_ipc_import(const void* handle_host, int64_t offset, void** ptr_host);
+/* Unmaps a pointer returned by sinkslot_ipc_import (same offset). */
+int sinkslot_ipc_close(void* ptr, int64_t offset);
+
+/* Scratch floats sinkslot_solve_shard needs for nr local rows and nc local
+ * columns. */
+int sinkslot_shard_work_floats(int64_t nr, int64_t nc, int64_t* floats_host);
+
+/* The Sinkhorn loop of sinkslot_solve_csr (variant 0 alternating, 1
+ * symmetric) for rank `rank` of `world` (<= 8) processes, one GPU each, that
+ * partition the rows and columns (no counterpart in the reference, whose loop
+ * runs on one device; sinkslot/sinkhorn_solvers.py:195-419).  This rank owns
+ * CSR rows [r0, r0+nr) (r_ptr rebased to 0, r_idx global column ids) and CSC
+ * columns [c0, c0+nc); r0 and c0 are multiples of 4.  phi_bufs_host[2g+k] /
+ * psi_bufs_host[2g+k] are rank g's potential buffers k = 0, 1 (n / m floats;
+ * k = 1 only for the symmetric variant) and flags_host[g] its `world` flag
+ * words (zeroed before the first call), as mapped in this process: local for
+ * g == rank, sinkslot_ipc_import'ed otherwise.  After each half-step the rank
+ * stores its slice into every peer's buffer and publishes a barrier epoch; the
+ * next half-step waits for all peers' epochs (bounded: a peer missing for ~4 s
+ * fails the call with status 2).  Runs iterations it0 .. it0+n_iters-1; the
+ * last carries check 0 none / 1 potential / 2 marginal and returns this rank's
+ * two check maxima (row, column side) in *check0_host, *check1_host.
+ * *cur_host: buffer index holding the current potentials (in/out);
+ * *epoch_host: last epoch used (in/out, 0 before the first call). */
+int sinkslot_solve_shard(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
+                         const float* r_lam, int64_t r_nnz, int64_t r0, int64_t nr,
+                         const void* r_tiles, int64_t r_tiles_bytes, const int32_t* c_ptr,
+                         const void* c_idx, int c_idx_bytes, const float* c_lam, int64_t c_nnz,
+                         int64_t c0, int64_t nc, const void* c_tiles, int64_t c_tiles_bytes,
+                         const float* log_a, const float* log_b, int64_t n, int64_t m,
+                         int variant, double alpha, int rank, int world,
+                         float* const* phi_bufs_host, float* const* psi_bufs_host,
+                         uint32_t* const* flags_host, int64_t it0, int64_t n_iters, int check,
+                         int* cur_host, uint32_t* epoch_host, float* work, int64_t work_floats,
+                         double* check0_host, double* check1_host, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Plan export and gradient
  * ------------------------------------------------------------------------- */
 

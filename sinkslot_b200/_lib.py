@@ -53,6 +53,15 @@ _SIGNATURES = {
                                   c_vp, c_i64, c_i64, c_int, c_int, c_i64, c_i64, c_i64, c_dbl,
                                   c_dbl, c_dbl, c_vp, c_i64, c_vp, c_i64,
                                   c_vp, c_vp, P_i64, P_int, P_dbl, c_vp],
+    "sinkslot_ipc_export": [c_vp, c_vp, P_i64],
+    "sinkslot_ipc_import": [c_vp, c_i64, ctypes.POINTER(c_vp)],
+    "sinkslot_ipc_close": [c_vp, c_i64],
+    "sinkslot_shard_work_floats": [c_i64, c_i64, P_i64],
+    "sinkslot_solve_shard": [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64,
+                             c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64,
+                             c_vp, c_vp, c_i64, c_i64, c_int, c_dbl, c_int, c_int,
+                             c_vp, c_vp, c_vp, c_i64, c_i64, c_int, P_int,
+                             ctypes.POINTER(ctypes.c_uint32), c_vp, c_i64, P_dbl, P_dbl, c_vp],
     "sinkslot_tiles_bytes": [c_i64, c_i64, c_i64, P_i64, P_i64],
     "sinkslot_tiles_geometry": [c_i64, c_i64, c_i64, P_int],
     "sinkslot_build_tiles": [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp,

@@ -1,0 +1,313 @@
+"""Row/column-partitioned SinkSLOT solve across the GPUs of one node.
+
+One process per GPU (``torch.distributed`` initialised by the caller, e.g.
+under ``torchrun``).  Every rank builds the same sliced support (the build is
+deterministic for identical inputs), keeps the CSR rows and CSC columns of its
+slice, and runs the Sinkhorn loop of ``sinkslot_solve`` on them in
+libsinkslot_b200.so (``sinkslot_solve_shard``): after every half-step the rank
+stores its potential slice straight into each peer's potential buffer (peer
+stores over NVLink through CUDA IPC mappings) and publishes a barrier epoch;
+the next half-step waits, bounded, until every peer's epoch has arrived.
+``torch.distributed`` carries only the set-up (IPC handles) and the stop
+checks (a max-reduction of two floats per check), so every rank takes the same
+stop decision at the same iteration, with the semantics of the single-GPU loop
+(reference: sinkslot/sinkhorn_solvers.py:195-419).
+
+The partition, the check schedule and the stop decisions are plain host code
+(``shard_bounds``, ``slice_csr``, ``plan_chunks``, ``drive``), exercised on CPU
+with gloo ranks by the tests.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from types import SimpleNamespace
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import call, ptr, stream_of
+from .sinkhorn_solvers import (SinkslotSolveResult, _idx_bytes, _resolve_stop_mode, _validate,
+                               build_tiles)
+from .solver import cost_and_lam, sot_plan_coo, to_csr
+
+MAX_RANKS = 8
+_CHECK_CODE = {"fixed": 0, "potential": 1, "marginal": 2}
+
+
+def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
+    """(start, count) of rank's slice of n items: equal slices of
+    ceil(n / world) rounded up to a multiple of 4 (16-byte aligned starts); the
+    last slices may be short or empty."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    size = -(-n // world)
+    size = (size + 3) // 4 * 4
+    if rank * size >= n:
+        return n // 4 * 4, 0  # an empty slice (start kept 4-aligned)
+    start = rank * size
+    return start, min(size, n - start)
+
+
+def slice_csr(ptr_: torch.Tensor, idx: torch.Tensor, vals: torch.Tensor, start: int,
+              count: int):
+    """Segments [start, start+count) of a CSR: (ptr rebased to 0 as int32, idx,
+    vals, nnz)."""
+    lo = int(ptr_[start])
+    hi = int(ptr_[start + count])
+    p = (ptr_[start:start + count + 1].to(torch.int64) - lo).to(torch.int32).contiguous()
+    return p, idx[lo:hi].contiguous(), vals[lo:hi].contiguous(), hi - lo
+
+
+def plan_chunks(mode: str, it: int, n_iters: int, max_iter: int, every: int) -> tuple[int, int]:
+    """(iterations, check) of the next chunk from iteration `it`: the chunk
+    ends at the next iteration that checks (check 1 potential / 2 marginal) or
+    at the end of the run (check 0).  The checking iterations are those of the
+    single-GPU loop: potential mode after iteration it+1 when (it+1) % every
+    == 0; marginal mode also at it+1 == max_iter; fixed mode never."""
+    if mode == "fixed":
+        return max(0, n_iters - it), 0
+    k = every - (it % every)
+    if it + k <= max_iter:
+        return k, _CHECK_CODE[mode]
+    left = max_iter - it
+    return left, (_CHECK_CODE[mode] if mode == "marginal" else 0)
+
+
+def _py_max(a: float, b: float) -> float:
+    return b if b > a else a  # Python's max(a, b)
+
+
+def drive(run_chunk: Callable[[int, int, int], tuple[float, float]],
+          reduce_max: Callable[[float, float], tuple[float, float]], mode: str, n_iters: int,
+          max_iter: int, every: int, tol: float, eps: float, alpha: float, variant: str):
+    """The stop logic of the single-GPU loop over chunks.  ``run_chunk(it0, k,
+    check)`` runs k iterations and returns this rank's two check maxima;
+    ``reduce_max`` makes them global.  Returns (iters_run, converged,
+    final_viol) as the reference loops do."""
+    if mode == "fixed":
+        if n_iters > 0:
+            run_chunk(0, n_iters, 0)
+        return int(n_iters), None, None
+    it = 0
+    value = math.inf
+    thr = tol if variant == "alternating" else alpha * tol
+    while it < max_iter:
+        k, check = plan_chunks(mode, it, n_iters, max_iter, every)
+        c0, c1 = run_chunk(it, k, check)
+        it += k
+        if check:
+            c0, c1 = reduce_max(c0, c1)
+            if mode == "potential":
+                value = eps * _py_max(c0, c1)
+                if value < thr:
+                    return it, True, value
+            else:
+                value = math.nan if (math.isnan(c0) or math.isnan(c1)) else max(c0, c1)
+                if value <= tol:
+                    return it, True, value
+    return it, False, value
+
+
+def _reduce_max_dist(group, device):
+    def reduce_max(c0: float, c1: float) -> tuple[float, float]:
+        nan = [math.isnan(c0), math.isnan(c1)]
+        t = torch.tensor([0.0 if nan[0] else c0, 0.0 if nan[1] else c1,
+                          float(nan[0]), float(nan[1])], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        v = t.tolist()
+        return (math.nan if v[2] else v[0]), (math.nan if v[3] else v[1])
+    return reduce_max
+
+
+class _SharedState:
+    """This rank's peer-writable buffer (phi[k] | psi[k] | flags) and the
+    mapped buffers of every peer."""
+
+    def __init__(self, n: int, m: int, nbuf: int, group, device):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n4 = (n + 3) // 4 * 4
+        self.m4 = (m + 3) // 4 * 4
+        self.nbuf = nbuf
+        self.floats = 2 * (self.n4 + self.m4) + 64  # flags: `world` words in the last 64
+        self.buf = torch.zeros(self.floats, dtype=torch.float32, device=device)
+        self.imported = []
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_int64(0)
+        with torch.cuda.device(device):
+            call("sinkslot_ipc_export", ptr(self.buf), handle, ctypes.byref(off))
+        mine = (bytes(handle), off.value)
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=group)
+        self.bases = []
+        for g, (h, o) in enumerate(every):
+            if g == self.rank:
+                self.bases.append(self.buf.data_ptr())
+                continue
+            p = ctypes.c_void_p(0)
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            with torch.cuda.device(device):
+                call("sinkslot_ipc_import", hb, o, ctypes.byref(p))
+            self.imported.append((p.value, o))
+            self.bases.append(p.value)
+
+    def pointers(self):
+        """(phi[2*world], psi[2*world], flags[world]) pointer arrays."""
+        W = self.world
+        phi = (ctypes.c_void_p * (2 * W))()
+        psi = (ctypes.c_void_p * (2 * W))()
+        flags = (ctypes.c_void_p * W)()
+        for g, b in enumerate(self.bases):
+            for k in range(2):
+                phi[2 * g + k] = b + 4 * k * self.n4 if k < self.nbuf else None
+                psi[2 * g + k] = b + 4 * (2 * self.n4 + k * self.m4) if k < self.nbuf else None
+            flags[g] = b + 4 * (2 * (self.n4 + self.m4))
+        return phi, psi, flags
+
+    def phi(self, k: int, n: int) -> torch.Tensor:
+        return self.buf[k * self.n4:k * self.n4 + n]
+
+    def psi(self, k: int, m: int) -> torch.Tensor:
+        o = 2 * self.n4 + k * self.m4
+        return self.buf[o:o + m]
+
+    def close(self):
+        for p, o in self.imported:
+            call("sinkslot_ipc_close", p, o)
+        self.imported = []
+
+
+class ShardedSolver:
+    """One rank's share of a partitioned solve, prepared once: the support (built
+    on every rank), this rank's CSR rows / CSC columns and their tiled layouts,
+    and the peer-mapped potential buffers.  ``solve`` runs a Sinkhorn loop from
+    zero potentials; ``close`` unmaps the peers' buffers (collective)."""
+
+    def __init__(self, X, Y, a, b, eps, L=64, seed=0, chunk=None, variant="alternating",
+                 alpha=0.5, group=None, tiled: bool = True):
+        if not dist.is_initialized():
+            raise RuntimeError("sharded solves need torch.distributed initialised")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > MAX_RANKS:
+            raise ValueError(f"at most {MAX_RANKS} ranks (one node), got {self.world}")
+        dev = X.device
+        self.dev = dev
+        n, m = X.shape[0], Y.shape[0]
+        self.n, self.m = n, m
+        self.eps, self.alpha, self.variant = eps, alpha, variant
+        self.rows, self.cols, self.S = sot_plan_coo(X, Y, a, b, L=L, seed=seed, chunk=chunk)
+        sizes = [None] * self.world
+        dist.all_gather_object(sizes, (n, m, self.rows.numel()), group=group)
+        if any(s != sizes[0] for s in sizes):
+            raise ValueError(f"ranks built different supports {sizes}: inputs must be identical")
+        lam, _ = cost_and_lam(X, Y, self.rows, self.cols, self.S, eps)
+        self.log_a, self.log_b = a.log().contiguous(), b.log().contiguous()
+        r_ptr, r_idx, r_lam, _ = to_csr(self.rows, self.cols, lam, n, narrow_key=True)
+        c_ptr, c_idx, c_lam, _ = to_csr(self.cols, self.rows, lam, m, narrow_key=True)
+        self.r0, self.nr = shard_bounds(n, self.world, self.rank)
+        self.c0, self.nc = shard_bounds(m, self.world, self.rank)
+        self.row = slice_csr(r_ptr, r_idx, r_lam, self.r0, self.nr)
+        self.col = slice_csr(c_ptr, c_idx, c_lam, self.c0, self.nc)
+        del r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, lam
+        use_tiles = tiled and self.nr > 0 and self.nc > 0
+        self.r_tiles = build_tiles(self.row[0], self.row[1], self.row[2], self.nr, m) \
+            if use_tiles else None
+        self.c_tiles = build_tiles(self.col[0], self.col[1], self.col[2], self.nc, n) \
+            if use_tiles else None
+        self.vcode = 0 if variant == "alternating" else 1
+        self.state = _SharedState(n, m, 1 + self.vcode, group, dev)
+        self.ptrs = self.state.pointers()
+        wf = _lib.out_i64()
+        call("sinkslot_shard_work_floats", self.nr, self.nc, ctypes.byref(wf))
+        self.work = torch.empty(wf.value, dtype=torch.float32, device=dev)
+        self.epoch = ctypes.c_uint32(0)
+        dist.barrier(group=group)  # every rank's buffer is zeroed and mapped
+
+    def _run_chunk(self, cur: ctypes.c_int, it0: int, k: int, check: int):
+        ch0, ch1 = ctypes.c_double(0.0), ctypes.c_double(0.0)
+        if k <= 0:
+            return 0.0, 0.0
+        (lr_ptr, lr_idx, lr_lam, r_nnz), (lc_ptr, lc_idx, lc_lam, c_nnz) = self.row, self.col
+        phi_p, psi_p, flag_p = self.ptrs
+        with torch.cuda.device(self.dev):
+            call("sinkslot_solve_shard", ptr(lr_ptr), ptr(lr_idx), _idx_bytes(lr_idx),
+                 ptr(lr_lam), r_nnz, self.r0, self.nr, ptr(self.r_tiles),
+                 self.r_tiles.numel() if self.r_tiles is not None else 0,
+                 ptr(lc_ptr), ptr(lc_idx), _idx_bytes(lc_idx), ptr(lc_lam), c_nnz, self.c0,
+                 self.nc, ptr(self.c_tiles),
+                 self.c_tiles.numel() if self.c_tiles is not None else 0,
+                 ptr(self.log_a), ptr(self.log_b), self.n, self.m, self.vcode,
+                 float(self.alpha), self.rank, self.world, phi_p, psi_p, flag_p, it0, k, check,
+                 ctypes.byref(cur), ctypes.byref(self.epoch), ptr(self.work), self.work.numel(),
+                 ctypes.byref(ch0), ctypes.byref(ch1), stream_of(self.dev))
+        return ch0.value, ch1.value
+
+    def solve(self, n_iters=200, stop_mode="fixed", stop_max_iter=20000, stop_tol=1e-6,
+              stop_check_every=5, copy_out: bool = True):
+        """(phi, psi, iters_run, converged, final_viol) from zero potentials,
+        with the stop semantics of the single-GPU loop.  All ranks call it."""
+        mode = _resolve_stop_mode(None if stop_mode == "fixed" else SimpleNamespace(
+            mode=stop_mode))
+        if mode == "potential" and self.eps is None:
+            raise ValueError("eps is required for stop.mode == 'potential'")
+        for k in range(1 + self.vcode):
+            self.state.phi(k, self.n).zero_()
+            self.state.psi(k, self.m).zero_()
+        cur = ctypes.c_int(0)
+        # peers may write this rank's buffers only after every rank has reset its own
+        dist.barrier(group=self.group)
+        it, converged, viol = drive(
+            lambda it0, k, check: self._run_chunk(cur, it0, k, check),
+            _reduce_max_dist(self.group, self.dev), mode, int(n_iters), int(stop_max_iter),
+            int(stop_check_every), float(stop_tol),
+            float(self.eps) if self.eps is not None else 0.0, float(self.alpha), self.variant)
+        phi = self.state.phi(cur.value, self.n)
+        psi = self.state.psi(cur.value, self.m)
+        if copy_out:
+            phi, psi = phi.clone(), psi.clone()
+        return phi, psi, it, converged, viol
+
+    def close(self):
+        # no rank may unmap or free a buffer a peer still writes
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        self.state.close()
+        dist.barrier(group=self.group)
+
+
+def sinkslot_solve_sharded(X, Y, a=None, b=None, eps=0.05, L=64, seed=0, n_iters=200,
+                           stop_mode="fixed", stop_max_iter=20000, stop_tol=1e-6,
+                           stop_check_every=5, chunk=None, backend="auto",
+                           variant="alternating", alpha=0.5, group=None,
+                           tiled: bool = True) -> SinkslotSolveResult:
+    """``sinkslot_solve`` with the Sinkhorn loop partitioned over the ranks of
+    ``group`` (default: the world), one GPU each.  Same arguments and result
+    as ``sinkslot_solve`` (every rank returns the full phi, psi and support);
+    X, Y, a, b must be identical on every rank."""
+    if not dist.is_initialized():
+        raise RuntimeError("sinkslot_solve_sharded needs torch.distributed initialised")
+    if a is None:
+        a = torch.full((X.shape[0],), 1.0 / X.shape[0], device=X.device, dtype=X.dtype)
+    if b is None:
+        b = torch.full((Y.shape[0],), 1.0 / Y.shape[0], device=Y.device, dtype=Y.dtype)
+    _validate(X, Y, a, b, backend, variant)
+    stop = None if stop_mode == "fixed" else SimpleNamespace(
+        mode=stop_mode, max_iter=stop_max_iter, tol=stop_tol, check_every=stop_check_every)
+    mode = _resolve_stop_mode(stop)
+    if mode == "potential" and eps is None:
+        raise ValueError("eps is required for stop.mode == 'potential'")
+    solver = ShardedSolver(X, Y, a, b, eps, L=L, seed=seed, chunk=chunk, variant=variant,
+                           alpha=alpha, group=group, tiled=tiled)
+    try:
+        phi, psi, it, converged, viol = solver.solve(n_iters, mode, stop_max_iter, stop_tol,
+                                                     stop_check_every)
+    finally:
+        solver.close()
+    return SinkslotSolveResult(phi, psi, solver.rows, solver.cols, solver.S, it, converged,
+                               viol)
