@@ -13,6 +13,25 @@ namespace sinkslot {
 enum OutMode { kOutPlain = 0, kOutBlend = 1, kOutNone = 2 };
 enum CheckMode { kChkNone = 0, kChkMarg = 1, kChkPot = 2 };
 
+// Copies of a half-step's output in other GPUs' potential buffers (mapped into
+// this process), indexed like `out`: the epilogue stores each value there too.
+constexpr int kMaxPeers = 7;
+struct PeerOut {
+  float* p[kMaxPeers];
+  int n;
+};
+
+// The end of a CTA of a half-step whose epilogue stored into peers: after all
+// of the CTA's threads (those in `bar`) are done, one thread makes their stores
+// visible system-wide and counts the CTA in *done (the publish step acquires
+// the count before it raises the peers' flags).
+__device__ __forceinline__ void peer_cta_done(const PeerOut& po, unsigned int* done) {
+  if (po.n > 0 && done != nullptr && threadIdx.x == 0) {
+    __threadfence_system();
+    atomicAdd(done, 1u);
+  }
+}
+
 // sinkhorn_solvers.py: the reference's `base - LSE` (:91-93), the symmetric
 // blend `(1 - alpha) * x + alpha * cand` (:361-363), the marginal proxy
 // `|a * exp(old - new) - a|` (:280-283, :405-412) and the potential change
@@ -20,14 +39,20 @@ enum CheckMode { kChkNone = 0, kChkMarg = 1, kChkPot = 2 };
 template <int OUT, int CHK>
 __device__ __forceinline__ void segment_epilogue(int64_t seg, float lse, const float* base,
                                                  const float* self_old, float* out, float w_old,
-                                                 float w_new, float* prev, uint32_t& chk_bits) {
+                                                 float w_new, float* prev, uint32_t& chk_bits,
+                                                 const PeerOut& po) {
   const float b = base ? base[seg] : 0.0f;
   const float res = base ? __fsub_rn(b, lse) : lse;
   float nv = res;
   float old = 0.0f;
   if (OUT == kOutBlend || CHK == kChkMarg) old = self_old[seg];
   if (OUT == kOutBlend) nv = __fadd_rn(__fmul_rn(w_old, old), __fmul_rn(w_new, res));
-  if (OUT != kOutNone) out[seg] = nv;
+  if (OUT != kOutNone) {
+    out[seg] = nv;
+#pragma unroll
+    for (int g = 0; g < kMaxPeers; ++g)  // constant indices: po stays in parameter space
+      if (g < po.n) po.p[g][seg] = nv;
+  }
   if (CHK == kChkMarg) {
     const float ea = expf(b);
     const float t = __fmul_rn(ea, expf(__fsub_rn(old, res)));

@@ -4,9 +4,11 @@
 // Rank g owns rows [r0, r0 + nr) of the CSR side and columns [c0, c0 + nc) of
 // the CSC side.  Every rank holds the full potentials phi (n) and psi (m) in a
 // buffer that its peers can write (a CUDA IPC mapping).  A half-step computes
-// the rank's own slice, stores it into the same place of every peer's buffer
-// (peer stores over NVLink), and publishes it: each block fences its stores at
-// system scope, the last block to finish writes the barrier epoch into a flag
+// the rank's own slice, and its epilogue stores every value both locally and
+// into the same place of every peer's buffer (peer stores over NVLink, spread
+// over the whole kernel, so the transfer overlaps the computation).  Each CTA
+// then fences its stores at system scope and counts itself; a one-thread
+// publish kernel acquires the count and writes the barrier epoch into a flag
 // word of every peer (release, system scope).  Before the next half-step reads
 // the other side's potential, a one-warp kernel waits until every peer's flag
 // for that epoch has arrived (acquire, system scope).  Every wait is bounded:
@@ -35,9 +37,6 @@ namespace sinkslot {
 constexpr int kMaxRanks = 8;
 constexpr long long kFlagWaitCycles = 8000000000ll;  // ~4 s at 2 GHz
 
-struct PeerSlices {
-  float* p[kMaxRanks];
-};
 struct PeerFlags {
   uint32_t* p[kMaxRanks];
 };
@@ -45,44 +44,36 @@ struct PeerFlags {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-// Copies src[0, count) to dst.p[g] for every peer g != rank, then the last
-// block to finish publishes `epoch` in flag slot `rank` of every peer.
-__global__ void push_publish_kernel(const float* __restrict__ src, int64_t count, PeerSlices dst,
-                                    PeerFlags flags, int rank, int world, uint32_t epoch,
-                                    unsigned int* done) {
-  const int64_t n4 = count >> 2;
-  const float4* s4 = reinterpret_cast<const float4*>(src);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 v = s4[i];
-#pragma unroll
-    for (int g = 0; g < kMaxRanks; ++g)
-      if (g < world && g != rank) reinterpret_cast<float4*>(dst.p[g])[i] = v;
-  }
-  if (blockIdx.x == 0) {
-    for (int64_t i = (n4 << 2) + threadIdx.x; i < count; i += blockDim.x) {
-      const float v = src[i];
-      for (int g = 0; g < world; ++g)
-        if (g != rank) dst.p[g][i] = v;
+// After the half-step's kernels, whose CTAs stored their outputs into the peers'
+// buffers and counted themselves in *done: acquires the count (all `expected`
+// CTAs), makes the stores visible system-wide and raises flag `rank` of every
+// peer to `epoch`.  One thread; bounded like every wait here.
+__global__ void publish_kernel(unsigned int* done, unsigned int expected, PeerFlags flags,
+                               int rank, int world, uint32_t epoch, int* err) {
+  if (threadIdx.x != 0) return;
+  const long long t0 = clock64();
+  while (ld_acquire_gpu(done) < expected) {
+    if (*(volatile int*)err != 0) break;
+    if (clock64() - t0 > kFlagWaitCycles) {
+      atomicCAS(err, 0, 6);
+      break;
     }
   }
+  *done = 0u;  // for the next half-step (its kernels are ordered after this one)
   __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int prev = atomicAdd(done, 1u);
-    if (prev == gridDim.x - 1) {
-      *done = 0u;  // for the next launch (ordered by the kernel boundary)
-      __threadfence_system();
-      for (int g = 0; g < world; ++g)
-        if (g != rank) st_release_sys(flags.p[g] + rank, epoch);
-    }
-  }
+  for (int g = 0; g < world; ++g)
+    if (g != rank) st_release_sys(flags.p[g] + rank, epoch);
 }
 
 // Waits until every peer has published `epoch` in this rank's flag words.
@@ -175,20 +166,14 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
   int c = *cur;
   uint32_t ep = *epoch;
 
-  // publish this rank's slice [off, off + len) of buffer `buf` of side `row`
-  auto publish = [&](bool row, int buf, int64_t off, int64_t len) -> int {
-    PeerSlices dst{};
-    PeerFlags fl{};
-    for (int g = 0; g < sp.world; ++g) {
-      dst.p[g] = (row ? sp.phi[g][buf] : sp.psi[g][buf]) + off;
-      fl.p[g] = sp.flags[g];
-    }
+  // after a half-step that stored into the peers (its kernels launched `ctas`
+  // CTAs): publish the next epoch, then wait for every peer's
+  auto publish = [&](unsigned int ctas) -> int {
     ++ep;
     if (sp.world > 1) {
-      const float* src = (row ? sp.phi[me][buf] : sp.psi[me][buf]) + off;
-      const int64_t n4 = std::max<int64_t>(1, len >> 2);
-      const int grid = (int)std::min<int64_t>(ceil_div64(n4, 256), 2 * (int64_t)num_sms());
-      push_publish_kernel<<<grid, 256, 0, st>>>(src, len, dst, fl, me, sp.world, ep, done);
+      PeerFlags fl{};
+      for (int g = 0; g < sp.world; ++g) fl.p[g] = sp.flags[g];
+      publish_kernel<<<1, 32, 0, st>>>(done, ctas, fl, me, sp.world, ep, perr);
       SINKSLOT_CHECK_LAUNCH();
       wait_epoch_kernel<<<1, 32, 0, st>>>(sp.flags[me], me, sp.world, ep, perr);
       SINKSLOT_CHECK_LAUNCH();
@@ -209,6 +194,13 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
     float* prev = row ? prev_phi : prev_psi;
     uint32_t* acc_side = acc + (row ? 0 : 1);
     const void* tiles = row ? sp.row_tiles : sp.col_tiles;
+    // the peers' copies of `out` (same offset in their buffer `nb`)
+    PeerOut po{};
+    po.n = 0;
+    if (out_mode != kOutNone)
+      for (int g = 0; g < sp.world; ++g)
+        if (g != me) po.p[po.n++] = (row ? sp.phi[g][nb] : sp.psi[g][nb]) + off;
+    unsigned int ctas = 0;
     if (side.nseg > 0) {
       if (tiles != nullptr && it > 0) {
         TiledHalfStep t;
@@ -230,7 +222,9 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
         t.fb_list = row ? fb_rows : fb_cols;
         t.fb_count_reset = fb_count + (row ? 1 : 0);
         t.err = perr;
-        SINKSLOT_TRY(tiled_half_step(t, out_mode, chk, st));
+        t.peers = po;
+        t.done = done;
+        SINKSLOT_TRY(tiled_half_step(t, out_mode, chk, st, &ctas));
       } else {
         HalfStep h = side;
         h.other = other;
@@ -241,11 +235,13 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
         h.w_new = w_new;
         h.self_old = self_cur;
         h.out = out;
-        SINKSLOT_TRY(half_step(h, out_mode, chk, st));
+        h.peers = po;
+        h.done = done;
+        SINKSLOT_TRY(half_step(h, out_mode, chk, st, &ctas));
       }
     }
     if (out_mode == kOutNone) return kOk;
-    return publish(row, nb, off, side.nseg);
+    return publish(ctas);
   };
 
   const int step_out = sp.variant == 0 ? kOutPlain : kOutBlend;

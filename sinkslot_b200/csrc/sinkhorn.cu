@@ -34,7 +34,8 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     const float* __restrict__ other, const float* __restrict__ selfpot,
     const float* __restrict__ base,
     const float* self_old, float* out, int64_t nseg, float w_old, float w_new, float* prev,
-    uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count) {
+    uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count,
+    const PeerOut po, unsigned int* done) {
   // self_old and out alias in the Gauss-Seidel variant (in-place update): no
   // __restrict__ on either, so the old value is read before the store.
   // With `list`, only the segments list[0 .. *list_count) are computed (the rows
@@ -96,10 +97,15 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     }
     if (lane == 0 && active) {
       const float lse = sm > 0.0f ? mx + logf(fmaxf(sm, FLT_MIN)) : -INFINITY;
-      segment_epilogue<OUT, CHK>(seg, lse, base, self_old, out, w_old, w_new, prev, chk_bits);
+      segment_epilogue<OUT, CHK>(seg, lse, base, self_old, out, w_old, w_new, prev, chk_bits,
+                                 po);
     }
   }
   check_reduce<CHK>(chk_bits, acc);
+  if (po.n > 0) {
+    __syncthreads();
+    peer_cta_done(po, done);
+  }
 }
 
 static int pick_group(int64_t nnz, int64_t nseg) {
@@ -110,7 +116,7 @@ static int pick_group(int64_t nnz, int64_t nseg) {
 }
 
 template <typename IT, int G>
-static void launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
+static unsigned launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
   const int64_t want = ceil_div64(h.nseg * G, kLseThreads);
   // a row-list launch does not know its count on the host: a small persistent
   // grid that exits at once when the list is empty
@@ -120,7 +126,7 @@ static void launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t st) 
 #define SINKSLOT_HS(OUTM, CHKM)                                                           \
   half_step_kernel<IT, G, OUTM, CHKM><<<grid, kLseThreads, 0, st>>>(                      \
       h.ptr, idx, h.lam, h.other, h.selfpot, h.base, h.self_old, h.out, h.nseg, h.w_old, h.w_new, \
-      h.prev, h.acc, h.list, h.list_count)
+      h.prev, h.acc, h.list, h.list_count, h.peers, h.done)
   if (out_mode == kOutPlain) {
     if (chk == kChkNone) SINKSLOT_HS(kOutPlain, kChkNone);
     else if (chk == kChkMarg) SINKSLOT_HS(kOutPlain, kChkMarg);
@@ -133,27 +139,31 @@ static void launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t st) 
     SINKSLOT_HS(kOutNone, kChkMarg);
   }
 #undef SINKSLOT_HS
+  return grid;
 }
 
 template <typename IT>
-static void launch_it(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
+static unsigned launch_it(const HalfStep& h, int out_mode, int chk, cudaStream_t st) {
   switch (h.group) {
-    case 4: launch_g<IT, 4>(h, out_mode, chk, st); break;
-    case 8: launch_g<IT, 8>(h, out_mode, chk, st); break;
-    case 16: launch_g<IT, 16>(h, out_mode, chk, st); break;
-    default: launch_g<IT, 32>(h, out_mode, chk, st); break;
+    case 4: return launch_g<IT, 4>(h, out_mode, chk, st);
+    case 8: return launch_g<IT, 8>(h, out_mode, chk, st);
+    case 16: return launch_g<IT, 16>(h, out_mode, chk, st);
+    default: return launch_g<IT, 32>(h, out_mode, chk, st);
   }
 }
 
-int half_step(const HalfStep& h0, int out_mode, int chk, cudaStream_t st) {
+int half_step(const HalfStep& h0, int out_mode, int chk, cudaStream_t st, unsigned int* ctas) {
   SINKSLOT_REQUIRE(h0.idx_bytes == 2 || h0.idx_bytes == 4, "half step: idx_bytes must be 2 or 4");
   SINKSLOT_REQUIRE(out_mode != kOutNone || chk == kChkMarg, "half step: check-only needs a check");
+  SINKSLOT_REQUIRE(h0.peers.n >= 0 && h0.peers.n <= kMaxPeers && (h0.peers.n == 0 || h0.done),
+                   "half step: bad peer outputs");
   if (h0.nseg <= 0) return kOk;
   HalfStep h = h0;
   if (h.group == 0) h.group = pick_group(h.nnz, h.nseg);
-  if (h.idx_bytes == 2) launch_it<int16_t>(h, out_mode, chk, st);
-  else launch_it<int32_t>(h, out_mode, chk, st);
+  const unsigned grid = h.idx_bytes == 2 ? launch_it<int16_t>(h, out_mode, chk, st)
+                                         : launch_it<int32_t>(h, out_mode, chk, st);
   SINKSLOT_CHECK_LAUNCH();
+  if (ctas) *ctas += grid;
   return kOk;
 }
 

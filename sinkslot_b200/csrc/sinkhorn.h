@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "epilogue.cuh"
 #include "tiled.h"
 
 namespace sinkslot {
@@ -28,10 +29,14 @@ struct HalfStep {
   uint32_t* acc = nullptr;
   const int* list = nullptr;        // optional: compute only these segments
   const int* list_count = nullptr;  // device count of `list`
+  PeerOut peers = {{}, 0};          // optional peer copies of `out`
+  unsigned int* done = nullptr;     // CTA counter for the peer publish step
 };
 
-// out_mode: 0 store, 1 alpha-blend store, 2 no store; chk: 0 none, 1 marginal, 2 potential
-int half_step(const HalfStep& h, int out_mode, int chk, cudaStream_t st);
+// out_mode: 0 store, 1 alpha-blend store, 2 no store; chk: 0 none, 1 marginal, 2 potential.
+// *ctas (optional) is increased by the number of CTAs launched.
+int half_step(const HalfStep& h, int out_mode, int chk, cudaStream_t st,
+              unsigned int* ctas = nullptr);
 
 struct SolveSpec {
   HalfStep row, col;

@@ -413,6 +413,8 @@ struct TKArgs {
   int* fb_list;
   int* fb_reset;
   int* err;
+  PeerOut peers;
+  unsigned int* done;
 };
 
 // State of panel row r: {sigma bits, high sum, low sum} at byte 12 r of the
@@ -642,11 +644,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       const float tot = (float)((double)q * kFixInv);
       const float lse = __fadd_rn(__uint_as_float(st[0]), logf(tot));
       segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
-                                 chk_bits);
+                                 chk_bits, a.peers);
     }
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
   }
   check_reduce<CHK>(chk_bits, a.acc);
+  if (a.peers.n > 0) {
+    // consumers only: the producer warp stored no potential
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
+    peer_cta_done(a.peers, a.done);
+  }
 }
 
 template <int OUT, int CHK>
@@ -667,7 +674,8 @@ static int launch_tiled(const TKArgs& a, size_t smem, cudaStream_t st) {
   return kOk;
 }
 
-int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st) {
+int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st,
+                    unsigned int* ctas) {
   SINKSLOT_REQUIRE(h.base != nullptr, "tiled half step: base is required");
   SINKSLOT_REQUIRE(h.fb_count && h.fb_list && h.err, "tiled half step: fallback list is required");
   SINKSLOT_REQUIRE(out_mode != kOutNone || chk == kChkMarg, "half step: check-only needs a check");
@@ -697,6 +705,8 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.fb_list = h.fb_list;
   a.fb_reset = h.fb_count_reset;
   a.err = h.err;
+  a.peers = h.peers;
+  a.done = h.done;
   const size_t smem = h.g.smem_bytes;
   if (out_mode == kOutPlain) {
     if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkNone>(a, smem, st)));
@@ -727,7 +737,10 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   x.acc = h.acc;
   x.list = h.fb_list;
   x.list_count = h.fb_count;
-  return half_step(x, out_mode, chk, st);
+  x.peers = h.peers;
+  x.done = h.done;
+  if (ctas) *ctas += (unsigned)std::min(h.g.P, num_sms());
+  return half_step(x, out_mode, chk, st, ctas);
 }
 
 }  // namespace sinkslot

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "epilogue.cuh"
+
 namespace sinkslot {
 
 // Geometry of a tiled layout: P panels of R rows; the gathered axis (length
@@ -46,9 +48,13 @@ struct TiledHalfStep {
   int* fb_list = nullptr;         // nseg entries
   int* fb_count_reset = nullptr;  // optional counter this launch zeroes (the other side's)
   int* err = nullptr;             // set nonzero when a pipeline wait times out
+  PeerOut peers = {{}, 0};        // optional peer copies of `out`
+  unsigned int* done = nullptr;   // CTA counter for the peer publish step
 };
 
-// tiled pass + exact pass over the rows it handed back
-int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st);
+// tiled pass + exact pass over the rows it handed back; *ctas (optional) is
+// increased by the number of CTAs launched
+int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st,
+                    unsigned int* ctas = nullptr);
 
 }  // namespace sinkslot
