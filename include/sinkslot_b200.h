@@ -135,8 +135,9 @@ int sinkslot_tiles_bytes(int64_t nseg, int64_t m_other, int64_t nnz, int64_t* la
  * Layout bytes: int64 header[8] | int64 tile_start[P*B + 1] | uint32
  * entries[cap][2] = {row within panel << 16 | column within block, lam bits},
  * each part 256-byte aligned; tile t = p*B + b holds entries [tile_start[t],
- * tile_start[t+1]) in CSR order, padded to a multiple of 32 with entries
- * {R << 16, -inf}; cap = nnz + 31*P*B. */
+ * tile_start[t+1]): the row's 1st entries in the tile by row, then its 2nd
+ * entries, ... (occurrences past 63 together), padded to a multiple of 32 with
+ * entries {R << 16, -inf}; cap = nnz + 31*P*B. */
 int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geom_host);
 
 /* Column-blocked layout of a CSR side for the shared-memory-staged half-step

@@ -9,8 +9,9 @@
 // shared-memory load.
 //
 // Layout (built once per solve from the CSR side): tile (p, b) = the entries of
-// panel p whose column lies in block b, in CSR order, padded to a multiple of 32
-// entries (one warp slab); per entry one uint2 {row within the panel << 16 |
+// panel p whose column lies in block b, ordered by the occurrence of their row
+// within the tile and then by row (see occ_key_kernel), padded to a multiple of
+// 32 entries (one warp slab); per entry one uint2 {row within the panel << 16 |
 // column within the block, fp32 lam bits}.  Padding names row R (a dummy row
 // of the panel state) with lam = -inf, so it adds an exact zero and the inner
 // loop needs no test for it.
@@ -132,7 +133,7 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   Carver bw(nullptr, 0);
   const int64_t e = std::max<int64_t>(nnz, 1);
   bw.take<uint32_t>(e);  // row id
-  bw.take<uint32_t>(e); bw.take<uint32_t>(e); bw.take<uint32_t>(e); bw.take<uint32_t>(e);
+  for (int i = 0; i < 6; ++i) bw.take<uint32_t>(e);  // keys / values of the two sorts
   const int64_t nh = radix_hist_elems(1, e);
   bw.take<int64_t>(std::max<int64_t>(nh, ntiles + 2));
   bw.take<int64_t>(scan_tmp_elems(std::max<int64_t>(nh, ntiles + 2)));
@@ -211,6 +212,30 @@ __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nn
   }
 }
 
+// Order inside a tile: by the occurrence of the row within the tile (its 1st,
+// 2nd, ... entry there), then by row.  A warp's 32 consecutive entries then
+// name 32 different rows, mostly consecutive ones, so their row-state updates
+// do not collide in shared memory (CSR order would put a row's entries side by
+// side: same address in neighbouring lanes).  The sums are exact fixed point,
+// so the order does not change any result.
+constexpr int kOccBits = 6;
+constexpr uint32_t kOccMax = (1u << kOccBits) - 1;
+
+// okey[q] = tile << kOccBits | occurrence of the entry's row within its tile
+// (entries sorted by tile, CSR order inside a tile; occurrences past kOccMax share it)
+__global__ void occ_key_kernel(const uint32_t* __restrict__ skey, const uint32_t* __restrict__ perm,
+                               const uint32_t* __restrict__ rowid, int64_t nnz,
+                               uint32_t* __restrict__ okey) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t t = skey[q];
+    const uint32_t r = rowid[perm[q]];
+    uint32_t kk = 0;
+    for (int64_t j = q - 1; j >= 0 && kk < kOccMax && skey[j] == t && rowid[perm[j]] == r; --j) ++kk;
+    okey[q] = (t << kOccBits) | kk;
+  }
+}
+
 // padding entries: the dummy row R, column 0, lam = -inf (a zero term)
 __global__ void fill_pad_kernel(uint2* __restrict__ ent, int64_t cap, int R) {
   const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
@@ -219,9 +244,12 @@ __global__ void fill_pad_kernel(uint2* __restrict__ ent, int64_t cap, int R) {
     ent[q] = pad;
 }
 
+// entry q of the final order: okey[q] its (tile, occurrence) key, order[q] its
+// position in the by-tile order, perm[] the CSR entry of that position
 template <typename IT>
-__global__ void tile_scatter_kernel(const uint32_t* __restrict__ perm,
-                                    const uint32_t* __restrict__ skey,
+__global__ void tile_scatter_kernel(const uint32_t* __restrict__ order,
+                                    const uint32_t* __restrict__ okey,
+                                    const uint32_t* __restrict__ perm,
                                     const uint32_t* __restrict__ rowid, const IT* __restrict__ idx,
                                     const float* __restrict__ lam, int64_t nnz, int R, int logW,
                                     const int64_t* __restrict__ ustart,
@@ -230,8 +258,8 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ perm,
   const uint32_t wmask = (1u << logW) - 1u;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
        q += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t k = perm[q];
-    const uint32_t t = skey[q];
+    const uint32_t t = okey[q] >> kOccBits;
+    const uint32_t k = perm[order[q]];
     const int64_t pos = tstart[t] + (q - ustart[t]);
     const uint32_t r = rowid[k];
     const uint32_t c = (uint32_t)idx[k];
@@ -244,7 +272,8 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   SINKSLOT_REQUIRE(idx_bytes == 2 || idx_bytes == 4, "build_tiles: idx_bytes must be 2 or 4");
   SINKSLOT_REQUIRE(g.nnz < (int64_t(1) << 32), "build_tiles: nnz must be < 2^32");
   SINKSLOT_REQUIRE(g.P > 0 && g.B > 0, "build_tiles: empty geometry");
-  SINKSLOT_REQUIRE((int64_t)g.P * g.B < (int64_t(1) << 31), "build_tiles: too many tiles");
+  SINKSLOT_REQUIRE((int64_t)g.P * g.B < (int64_t(1) << (32 - kOccBits)),
+                   "build_tiles: too many tiles");
   LayoutPtrs L = carve_layout(layout, g);
   Carver cv(ws, ws_bytes);
   const int64_t e = std::max<int64_t>(g.nnz, 1);
@@ -254,6 +283,8 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   uint32_t* v1 = cv.take<uint32_t>(e);
   uint32_t* k2 = cv.take<uint32_t>(e);
   uint32_t* v2 = cv.take<uint32_t>(e);
+  uint32_t* k3 = cv.take<uint32_t>(e);
+  uint32_t* v3 = cv.take<uint32_t>(e);
   const int64_t nh = std::max<int64_t>(radix_hist_elems(1, e), ntiles + 2);
   int64_t* hist = cv.take<int64_t>(nh);
   int64_t* stmp = cv.take<int64_t>(scan_tmp_elems(nh));
@@ -290,14 +321,25 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
                                                               L.tstart);
   SINKSLOT_CHECK_LAUNCH();
   SINKSLOT_TRY(scan_exclusive_i64(L.tstart, ntiles, stmp, L.tstart + ntiles, st));
+  // second stable sort: by (tile, occurrence of the row in the tile)
+  uint32_t* okey = alt ? k1 : k2;  // the pair the first sort left free
+  uint32_t* oval = alt ? v1 : v2;
+  occ_key_kernel<<<grid_t(g.nnz, 256), 256, 0, st>>>(skey, perm, rowid, g.nnz, okey);
+  SINKSLOT_CHECK_LAUNCH();
+  bool alt2 = false;
+  SINKSLOT_TRY(radix_sort_pairs<uint32_t>(
+      okey, oval, k3, v3, true, 1, g.nnz,
+      bits_for((uint64_t)std::max<int64_t>(ntiles, 2)) + kOccBits, hist, stmp, &alt2, st));
+  const uint32_t* okey_s = alt2 ? k3 : okey;
+  const uint32_t* order = alt2 ? v3 : oval;
   if (idx_bytes == 2)
     tile_scatter_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-        perm, skey, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
-        L.tstart, L.ent);
+        order, okey_s, perm, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW,
+        ustart, L.tstart, L.ent);
   else
     tile_scatter_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-        perm, skey, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
-        L.tstart, L.ent);
+        order, okey_s, perm, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW,
+        ustart, L.tstart, L.ent);
   SINKSLOT_CHECK_LAUNCH();
   return kOk;
 }

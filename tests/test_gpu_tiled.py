@@ -81,7 +81,14 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     lam_h = lam.cpu().numpy()
     row_of = np.repeat(np.arange(n), np.diff(ptr_h))
     tile_of = (row_of // R) * B + (idx_h >> logW)
-    order = np.argsort(tile_of, kind="stable")
+    by_tile = np.argsort(tile_of, kind="stable")
+    # inside a tile: by the occurrence of the row there (capped at 63), then by row
+    t_s, r_s = tile_of[by_tile], row_of[by_tile]
+    occ = np.zeros(nnz, dtype=np.int64)
+    for q in range(1, nnz):
+        if t_s[q] == t_s[q - 1] and r_s[q] == r_s[q - 1]:
+            occ[q] = occ[q - 1] + 1
+    order = by_tile[np.lexsort((np.arange(nnz), np.minimum(occ, 63), t_s))]
     counts = np.bincount(tile_of, minlength=T)
     padded = (counts + 31) // 32 * 32
     np.testing.assert_array_equal(tstart, np.concatenate([[0], np.cumsum(padded)]))
