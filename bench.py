@@ -175,7 +175,7 @@ def run_b200(args):
     import sinkslot_b200
     from sinkslot_b200 import sinkslot_solve
     from sinkslot_b200.sinkhorn_solvers import (build_tiles, seg_lse_online,
-                                                sinkslot_alternating_b200)
+                                                sinkslot_alternating_b200, tiles_pay_off)
     from sinkslot_b200.solver import cost_and_lam, sot_plan_coo, to_csr
 
     world, rank, local = dist_setup(args.gpus)
@@ -196,8 +196,12 @@ def run_b200(args):
     lam, _ = cost_and_lam(X, Y, rows, cols, S, w["eps"])
     r_ptr, r_idx, r_lam, _ = to_csr(rows, cols, lam, w["n"])
     c_ptr, c_idx, c_lam, _ = to_csr(cols, rows, lam, w["m"])
-    tiles = None if args.plain else (build_tiles(r_ptr, r_idx, r_lam, w["n"], w["m"]),
-                                     build_tiles(c_ptr, c_idx, c_lam, w["m"], w["n"]))
+    nnz0 = int(rows.numel())
+    tiles = None if args.plain else (
+        build_tiles(r_ptr, r_idx, r_lam, w["n"], w["m"]) if tiles_pay_off(w["n"], w["m"], nnz0)
+        else None,
+        build_tiles(c_ptr, c_idx, c_lam, w["m"], w["n"]) if tiles_pay_off(w["m"], w["n"], nnz0)
+        else None)
     log_a, log_b = A.log(), B.log()
     torch.cuda.synchronize(dev)
     setup_ms = (time.perf_counter() - t0) * 1e3

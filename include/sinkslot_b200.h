@@ -153,9 +153,10 @@ int sinkslot_build_tiles(const int32_t* indptr, const void* idx, int idx_bytes, 
  * (variant 1), sinkslot/sinkhorn_solvers.py:195-419, with the semantics of
  * their torch twins (:443-588).  stop_mode: 0 fixed (n_iters), 1 potential,
  * 2 marginal (up to max_iter, checked every check_every).  r_tiles / c_tiles
- * (both or neither) are layouts from sinkslot_build_tiles of the two sides;
- * with them every iteration after the first runs the shared-memory-staged
- * half-step.  phi (n), psi (m) receive the absorbed potentials.
+ * (each nullable) are layouts from sinkslot_build_tiles of the two sides; a
+ * side with one runs the shared-memory-staged half-step in every iteration
+ * after the first, a side without the exact kernel.  phi (n), psi (m) receive
+ * the absorbed potentials.
  * *converged_host: -1 (fixed mode), 0 or 1; *final_viol_host: NaN in fixed
  * mode. */
 int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,

@@ -165,14 +165,17 @@ int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                    "solve_csr: null argument");
   SINKSLOT_REQUIRE(nnz == 0 || (r_idx && r_lam && c_idx && c_lam), "solve_csr: null argument");
   SolveSpec sp;
-  if (r_tiles || c_tiles) {
-    SINKSLOT_REQUIRE(r_tiles && c_tiles, "solve_csr: give both tiled layouts or neither");
+  // either side may run tiled or exact (a null layout)
+  if (r_tiles) {
     sp.row_geom = tile_geom(n, m, nnz, num_sms());
-    sp.col_geom = tile_geom(m, n, nnz, num_sms());
-    SINKSLOT_REQUIRE(r_tiles_bytes >= (int64_t)sp.row_geom.layout_bytes &&
-                         c_tiles_bytes >= (int64_t)sp.col_geom.layout_bytes,
+    SINKSLOT_REQUIRE(r_tiles_bytes >= (int64_t)sp.row_geom.layout_bytes,
                      "solve_csr: tiled layout buffer too small");
     sp.row_tiles = r_tiles;
+  }
+  if (c_tiles) {
+    sp.col_geom = tile_geom(m, n, nnz, num_sms());
+    SINKSLOT_REQUIRE(c_tiles_bytes >= (int64_t)sp.col_geom.layout_bytes,
+                     "solve_csr: tiled layout buffer too small");
     sp.col_tiles = c_tiles;
   }
   sp.row.ptr = r_ptr;

@@ -139,8 +139,6 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
                    "solve_shard: work buffer too small");
   SINKSLOT_REQUIRE(sp.r0 % 4 == 0 && sp.c0 % 4 == 0,
                    "solve_shard: slice starts must be multiples of 4");
-  SINKSLOT_REQUIRE((sp.row_tiles == nullptr) == (sp.col_tiles == nullptr),
-                   "solve_shard: give tiled layouts for both sides or neither");
   for (int g = 0; g < sp.world; ++g)
     SINKSLOT_REQUIRE(sp.phi[g][0] && sp.psi[g][0] && sp.flags[g] &&
                          (sp.variant == 0 || (sp.phi[g][1] && sp.psi[g][1])),
@@ -221,6 +219,10 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
         t.fb_count = fb_count + (row ? 0 : 1);
         t.fb_list = row ? fb_rows : fb_cols;
         t.fb_count_reset = fb_count + (row ? 1 : 0);
+        // This side's counter is zeroed by the other side's tiled launch; when the
+        // other side runs exact, zero it here.
+        if ((row ? sp.col_tiles : sp.row_tiles) == nullptr)
+          SINKSLOT_CUDA_TRY(cudaMemsetAsync(t.fb_count, 0, sizeof(int), st));
         t.err = perr;
         t.peers = po;
         t.done = done;
@@ -379,15 +381,19 @@ extern "C" int sinkslot_solve_shard(
   sp.col.nnz = c_nnz;
   sp.r0 = r0;
   sp.c0 = c0;
-  if (r_tiles || c_tiles) {
-    SINKSLOT_REQUIRE(r_tiles && c_tiles && nr > 0 && nc > 0,
-                     "solve_shard: give both tiled layouts (non-empty slices) or neither");
+  // either side may run tiled or exact (a null layout)
+  if (r_tiles) {
+    SINKSLOT_REQUIRE(nr > 0, "solve_shard: a tiled layout needs a non-empty row slice");
     sp.row_geom = tile_geom(nr, m, r_nnz, num_sms());
-    sp.col_geom = tile_geom(nc, n, c_nnz, num_sms());
-    SINKSLOT_REQUIRE(r_tiles_bytes >= (int64_t)sp.row_geom.layout_bytes &&
-                         c_tiles_bytes >= (int64_t)sp.col_geom.layout_bytes,
+    SINKSLOT_REQUIRE(r_tiles_bytes >= (int64_t)sp.row_geom.layout_bytes,
                      "solve_shard: tiled layout buffer too small");
     sp.row_tiles = r_tiles;
+  }
+  if (c_tiles) {
+    SINKSLOT_REQUIRE(nc > 0, "solve_shard: a tiled layout needs a non-empty column slice");
+    sp.col_geom = tile_geom(nc, n, c_nnz, num_sms());
+    SINKSLOT_REQUIRE(c_tiles_bytes >= (int64_t)sp.col_geom.layout_bytes,
+                     "solve_shard: tiled layout buffer too small");
     sp.col_tiles = c_tiles;
   }
   sp.log_a = log_a;

@@ -209,8 +209,6 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   SINKSLOT_REQUIRE(sp.mode >= 0 && sp.mode <= 2, "unknown stop.mode");
   SINKSLOT_REQUIRE(sp.mode == 0 || sp.check_every >= 1, "solve: check_every must be >= 1");
   SINKSLOT_REQUIRE(work_floats >= (int64_t)solve_work_floats(n, m), "solve: work buffer too small");
-  SINKSLOT_REQUIRE((sp.row_tiles == nullptr) == (sp.col_tiles == nullptr),
-                   "solve: give tiled layouts for both sides or neither");
   // work (each part 16-byte aligned): phi_next (n) | psi_next (m) | prev_phi (n) |
   //       prev_psi (m) | 64 words: [0,1] check maxima, [2,3] handed-back row
   //       counts, [4] pipeline error | handed-back row lists (n, m)
@@ -243,7 +241,7 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   // (the starting potentials are no estimate of the LSE the tiled pass needs as
   // its stabiliser); later ones the tiled pass plus the exact pass over the rows
   // it hands back.
-  auto side_step = [&](bool row, int out_mode, int chk) {
+  auto side_step = [&](bool row, int out_mode, int chk) -> int {
     const HalfStep& side = row ? sp.row : sp.col;
     float* self_cur = row ? phi_cur : psi_cur;
     float* self_nx = row ? phi_nx : psi_nx;
@@ -272,6 +270,10 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
       t.fb_count = fb_count + (row ? 0 : 1);
       t.fb_list = row ? fb_rows : fb_cols;
       t.fb_count_reset = fb_count + (row ? 1 : 0);
+      // This side's counter is zeroed by the other side's tiled launch; when the
+      // other side runs exact, zero it here.
+      if ((row ? sp.col_tiles : sp.row_tiles) == nullptr)
+        SINKSLOT_CUDA_TRY(cudaMemsetAsync(t.fb_count, 0, sizeof(int), st));
       t.err = perr;
       return tiled_half_step(t, out_mode, chk, st);
     }
@@ -362,7 +364,7 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   if (psi_cur != psi)
     SINKSLOT_CUDA_TRY(cudaMemcpyAsync(psi, psi_cur, m * sizeof(float), cudaMemcpyDeviceToDevice, st));
   *iters_run = it;
-  if (sp.row_tiles) return read_err(perr, st);
+  if (sp.row_tiles || sp.col_tiles) return read_err(perr, st);
   return kOk;
 }
 

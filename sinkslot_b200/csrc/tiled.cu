@@ -84,6 +84,12 @@ constexpr int kLoBits = 20;
 constexpr long long kWaitCycles = 8000000000ll;  // ~4 s at 2 GHz: a wait this long is a bug
 
 constexpr int kSlab = 32;  // tiles are padded to whole warp slabs of entries
+// slabs a consumer warp loads and processes together (its next tile's first
+// group is in flight while it works on the current tile)
+#ifndef SINKSLOT_TILE_GROUP
+#define SINKSLOT_TILE_GROUP 4
+#endif
+constexpr int kGroup = SINKSLOT_TILE_GROUP;
 
 // Shared memory of the per-row state: rows 0..R-1 of the panel and a dummy row R
 // (the target of tile padding), 12 bytes each at offset 12 r: sigma (float),
@@ -501,38 +507,41 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Lane `lane` of slabs g .. g+3 of the tile whose entries start at e0 (only the
-// slabs below nsl are loaded): coalesced 8-byte streaming loads, 256 bytes per
-// slab.
+// Lane `lane` of slabs g .. g+kGroup-1 of the tile whose entries start at e0
+// (only the slabs below nsl are loaded): coalesced 8-byte streaming loads, 256
+// bytes per slab.
 __device__ __forceinline__ void load_group(const uint2* ent, int64_t e0, int nsl, int g, int lane,
-                                           uint2 (&e)[4]) {
+                                           uint2 (&e)[kGroup]) {
   const uint2* p = ent + e0 + (int64_t)g * kSlab + lane;
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int j = 0; j < kGroup; ++j)
     if (g + j < nsl) e[j] = ld_stream(p + j * kSlab);
 }
 
-// The terms of a group of `cnt` (>= 1) slabs; when all four exist one vote per
-// group checks the cap of its 128 terms.
+// The terms of a group of `cnt` (>= 1) slabs; when the whole group exists one
+// vote checks the cap of its terms.
 __device__ __forceinline__ void process_group(unsigned char* smem, uint32_t* flags,
-                                              const float* cur, const uint2 (&e)[4], int cnt,
+                                              const float* cur, const uint2 (&e)[kGroup], int cnt,
                                               float capd) {
-  if (cnt >= 4) {
-    uint32_t* st[4];
-    float d[4];
+  if (cnt >= kGroup) {
+    uint32_t* st[kGroup];
+    float d[kGroup];
+    bool in_cap = true;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) d[j] = entry_exponent(smem, cur, e[j], st[j]);
-    const bool in_cap = (d[0] <= capd) & (d[1] <= capd) & (d[2] <= capd) & (d[3] <= capd);
+    for (int j = 0; j < kGroup; ++j) {
+      d[j] = entry_exponent(smem, cur, e[j], st[j]);
+      in_cap &= d[j] <= capd;
+    }
     if (!__all_sync(0xffffffffu, in_cap)) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < kGroup; ++j)
         if (!(d[j] <= capd)) flag_row(flags, e[j]);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) accumulate(st[j], d[j]);
+    for (int j = 0; j < kGroup; ++j) accumulate(st[j], d[j]);
   } else {
 #pragma unroll
-    for (int j = 0; j < 3; ++j) {
+    for (int j = 0; j < kGroup - 1; ++j) {
       if (j < cnt) {
         uint32_t* st;
         const float d = entry_exponent(smem, cur, e[j], st);
@@ -645,26 +654,26 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     }
     for (int r = tid; r < (a.R + 1 + 31) / 32; r += kConsumers) flags[r] = 0u;
     // Tile b holds slabs [e0, e1) / 32 of the layout.  Warp w takes groups of
-    // four consecutive slabs starting at 4w, 4w + 4*31, ...; its first group of
+    // kGroup consecutive slabs starting at kGroup*w, kGroup*(w + warps), ...; its first group of
     // the next tile is loaded while the current tile is processed.
     int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
-    uint2 en[4];
-    load_group(a.ent, e0, (int)((e1 - e0) / kSlab), 4 * warp, lane, en);
+    uint2 en[kGroup];
+    load_group(a.ent, e0, (int)((e1 - e0) / kSlab), kGroup * warp, lane, en);
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     for (int b = 0; ok && b < a.B; ++b) {
       const int nsl = (int)((e1 - e0) / kSlab);
-      uint2 e[4];
+      uint2 e[kGroup];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) e[j] = en[j];
+      for (int j = 0; j < kGroup; ++j) e[j] = en[j];
       const int64_t f0 = e1;
       const int64_t f1 = b + 1 < a.B ? a.tstart[pb + b + 2] : e1;
-      load_group(a.ent, f0, (int)((f1 - f0) / kSlab), 4 * warp, lane, en);
+      load_group(a.ent, f0, (int)((f1 - f0) / kSlab), kGroup * warp, lane, en);
       const int s = sb;
       if (!(ok = warp_wait(pot_full(s), ub, abort_w, a.err, 3))) break;
       if (++sb == kStages) { sb = 0; ub ^= 1u; }
       const float* cur = pot + (size_t)s * W;
-      for (int g = 4 * warp; g < nsl; g += 4 * kConsumerWarps) {
-        if (g != 4 * warp) load_group(a.ent, e0, nsl, g, lane, e);
+      for (int g = kGroup * warp; g < nsl; g += kGroup * kConsumerWarps) {
+        if (g != kGroup * warp) load_group(a.ent, e0, nsl, g, lane, e);
         process_group(smem, flags, cur, e, nsl - g, capd);
       }
       __syncwarp();

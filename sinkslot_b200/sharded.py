@@ -31,7 +31,7 @@ import torch.distributed as dist
 from . import _lib
 from ._lib import call, ptr, stream_of
 from .sinkhorn_solvers import (SinkslotSolveResult, _idx_bytes, _resolve_stop_mode, _validate,
-                               build_tiles)
+                               build_tiles, tiles_pay_off)
 from .solver import cost_and_lam, sot_plan_coo, to_csr
 
 MAX_RANKS = 8
@@ -215,11 +215,10 @@ class ShardedSolver:
         self.row = slice_csr(r_ptr, r_idx, r_lam, self.r0, self.nr)
         self.col = slice_csr(c_ptr, c_idx, c_lam, self.c0, self.nc)
         del r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, lam
-        use_tiles = tiled and self.nr > 0 and self.nc > 0
         self.r_tiles = build_tiles(self.row[0], self.row[1], self.row[2], self.nr, m) \
-            if use_tiles else None
+            if tiled and tiles_pay_off(self.nr, m, self.row[3]) else None
         self.c_tiles = build_tiles(self.col[0], self.col[1], self.col[2], self.nc, n) \
-            if use_tiles else None
+            if tiled and tiles_pay_off(self.nc, n, self.col[3]) else None
         self.vcode = 0 if variant == "alternating" else 1
         self.state = _SharedState(n, m, 1 + self.vcode, group, dev)
         self.ptrs = self.state.pointers()

@@ -85,6 +85,28 @@ def _resolve_stop_mode(stop):
     return mode
 
 
+# A side runs the shared-memory-staged half-step when staging the gathered
+# potential costs at most this many times its entry stream: each of the P
+# panels copies all m_other potentials into shared memory per half-step
+# (P * m_other * 4 bytes) while the entries are read once (nnz * 8 bytes).
+# Measured on B200 (N = 2^20 on one GPU and 2^20 x 2^21 slices on two): the
+# tiled half-step costs ~165 us per GB of entries plus ~69 us per GB of
+# staging, the exact kernel ~590 us per GB of entries, so the tiled pass wins
+# below a ratio of ~6 (large gathered axes, e.g. N = 2^24, or row slices of a
+# many-GPU partition, run the exact kernel).
+TILE_STAGING_RATIO = 6.0
+
+
+def tiles_pay_off(nseg: int, m_other: int, nnz: int) -> bool:
+    """Whether a side of nseg segments gathering from m_other potentials with
+    nnz entries should run the tiled half-step (see TILE_STAGING_RATIO)."""
+    if nseg <= 0 or m_other <= 0 or nnz <= 0:
+        return False
+    geom = (ctypes.c_int * 5)()
+    call("sinkslot_tiles_geometry", nseg, m_other, nnz, geom)
+    return geom[0] * m_other * 4 <= TILE_STAGING_RATIO * nnz * 8
+
+
 def build_tiles(indptr, idx, lam, nseg: int, m_other: int) -> torch.Tensor:
     """Column-blocked layout of one CSR side (device bytes) for the half-step
     that stages the gathered potential in shared memory."""
@@ -232,7 +254,9 @@ def sinkslot_solve(X: Float[torch.Tensor, "n d"], Y: Float[torch.Tensor, "m d"],
     log_a, log_b = a.log(), b.log()
     r_ptr, r_idx, r_lam, _ = to_csr(rows, cols, lam, n, narrow_key=True)
     c_ptr, c_idx, c_lam, _ = to_csr(cols, rows, lam, m, narrow_key=True)
-    tiles = (build_tiles(r_ptr, r_idx, r_lam, n, m), build_tiles(c_ptr, c_idx, c_lam, m, n))
+    nnz = rows.numel()
+    tiles = (build_tiles(r_ptr, r_idx, r_lam, n, m) if tiles_pay_off(n, m, nnz) else None,
+             build_tiles(c_ptr, c_idx, c_lam, m, n) if tiles_pay_off(m, n, nnz) else None)
     if variant == "symmetric":
         phi, psi, it, converged, viol = sinkslot_symmetric_b200(
             r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters, stop, eps,

@@ -150,3 +150,23 @@ def test_tiled_matches_exact_stop_modes(cuda, mode, tol, variant):
     c = float((pt - pe).double().mean())
     torch.testing.assert_close(pt - c, pe, rtol=0, atol=5e-3)
     torch.testing.assert_close(qt + c, qe, rtol=0, atol=5e-3)
+
+
+@pytest.mark.parametrize("sides", ["row", "col"])
+@pytest.mark.parametrize("variant", ["alternating", "symmetric"])
+def test_one_side_tiled_matches_exact(cuda, sides, variant):
+    """One side tiled, the other exact (the choice large gathered axes make):
+    the handed-back row counters of the tiled side are reset every half-step."""
+    from sinkslot_b200.sinkhorn_solvers import (build_tiles, sinkslot_alternating_b200,
+                                                sinkslot_symmetric_b200)
+    n, m = 20000, 30000
+    csr = _problem(n, m, 2, 7, "dirichlet", cuda, L=48, eps=0.002)  # rows are handed back
+    rt = build_tiles(csr[0], csr[1], csr[2], n, m) if sides == "row" else None
+    ct = build_tiles(csr[3], csr[4], csr[5], m, n) if sides == "col" else None
+    fn = sinkslot_alternating_b200 if variant == "alternating" else sinkslot_symmetric_b200
+    pe, qe, *_ = fn(*csr, 150)
+    pt, qt, *_ = fn(*csr, 150, tiles=(rt, ct))
+    atol_p = ATOL + 2e-7 * float(pe.abs().max())
+    atol_q = ATOL + 2e-7 * float(qe.abs().max())
+    torch.testing.assert_close(pt, pe, rtol=RTOL, atol=atol_p)
+    torch.testing.assert_close(qt, qe, rtol=RTOL, atol=atol_q)
