@@ -391,15 +391,21 @@ def run_b200_sharded(args, world, rank, local):
     xh, yh, ah, bh = (t.pin_memory() for t in (x, y, a, b))
     phi_h = torch.empty(w["n"]).pin_memory()
     psi_h = torch.empty(w["m"]).pin_memory()
+
+    def e2e_step():
+        r = sinkslot_solve_sharded(xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True),
+                                   ah.to(dev, non_blocking=True), bh.to(dev, non_blocking=True),
+                                   w["eps"], w["L"], w["proj_seed"], w["n_iters"])
+        phi_h.copy_(r.phi, non_blocking=True)
+        psi_h.copy_(r.psi, non_blocking=True)
+
+    e2e_step()  # untimed: first-call set-up (IPC mappings, library state)
+    torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
     q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     q0.record(stream)
-    r = sinkslot_solve_sharded(xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True),
-                               ah.to(dev, non_blocking=True), bh.to(dev, non_blocking=True),
-                               w["eps"], w["L"], w["proj_seed"], w["n_iters"])
-    phi_h.copy_(r.phi, non_blocking=True)
-    psi_h.copy_(r.psi, non_blocking=True)
+    e2e_step()
     q1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
