@@ -1,6 +1,8 @@
 // primitives.cu -- device-wide exclusive scan and a stable, segmented LSD radix
-// sort (8-bit digits).  Both are HBM-bound integer passes: tiles of 4096 keys,
-// 256-thread blocks, warp-level match/ballot ranking for stability.
+// sort (8-bit digits).  Both are HBM-bound integer passes: tiles of 2048 keys,
+// 256-thread blocks, warp-level match/ballot ranking for stability, and each
+// tile reordered by digit in shared memory before it is written out, so the
+// stores of a digit's run are coalesced.
 #include "common.cuh"
 #include "primitives.h"
 
@@ -118,9 +120,13 @@ int scan_exclusive_i64(int64_t* data, int64_t n, int64_t* tmp, int64_t* total,
 // --------------------------------------------------------------------------
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 16;
-constexpr int kSortTile = kSortThreads * kSortItems;  // 4096 keys per tile
+#ifndef SINKSLOT_SORT_ITEMS
+#define SINKSLOT_SORT_ITEMS 8
+#endif
+constexpr int kSortItems = SINKSLOT_SORT_ITEMS;  // keys per thread of a tile
+constexpr int kSortTile = kSortThreads * kSortItems;  // keys per tile
 constexpr int kRadix = 256;
+static_assert(kSortThreads == kRadix, "the scatter kernel gives each thread one digit");
 
 int64_t radix_hist_elems(int64_t nseg, int64_t seglen) {
   return nseg * kRadix * ceil_div64(seglen, kSortTile);
@@ -155,19 +161,64 @@ __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const K* __res
   }
 }
 
+// Exclusive scan of one value per thread over the 256 threads of the block.
+__device__ __forceinline__ uint32_t block_excl_scan256(uint32_t v, uint32_t* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = lane < kSortWarps ? warp_tot[lane] : 0u;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < kSortWarps; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < kSortWarps) warp_tot[lane] = wi - w;
+  }
+  __syncthreads();
+  return warp_tot[warp] + incl - v;
+}
+
+// Dynamic shared memory of the scatter kernel: the tile's keys and values in
+// digit order (stable), then per-(warp, digit) counts, per-digit tile starts
+// and global run starts.
+template <typename K>
+constexpr size_t scatter_smem() {
+  return (size_t)kSortTile * (sizeof(K) + 4) + (size_t)kSortWarps * kRadix * 4 + kRadix * 4 +
+         kRadix * 8 + 64;
+}
+
+// One pass: the tile's keys are ranked (stable: warp match by digit, warps in
+// order), placed in shared memory in digit order, and written out run by run,
+// so consecutive threads store consecutive addresses of each digit's run.
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, K* __restrict__ keys_out,
     uint32_t* __restrict__ vals_out, int64_t seglen, int ntiles, int shift,
     const int64_t* __restrict__ offs) {
-  __shared__ uint32_t wcnt[kSortWarps][kRadix];
-  __shared__ int64_t wbase[kSortWarps][kRadix];
+  extern __shared__ __align__(16) unsigned char sm[];
+  K* skey = reinterpret_cast<K*>(sm);
+  uint32_t* sval = reinterpret_cast<uint32_t*>(sm + (size_t)kSortTile * sizeof(K));
+  uint32_t(*wcnt)[kRadix] = reinterpret_cast<uint32_t(*)[kRadix]>(
+      sm + (size_t)kSortTile * (sizeof(K) + 4));
+  uint32_t* dstart = reinterpret_cast<uint32_t*>(&wcnt[kSortWarps][0]);
+  int64_t* gbase = reinterpret_cast<int64_t*>(dstart + kRadix);
+  uint32_t* warp_tot = reinterpret_cast<uint32_t*>(gbase + kRadix);
   const int seg = blockIdx.y, tile = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&wcnt[0][0])[i] = 0;
   __syncthreads();
   const int64_t segbase = (int64_t)seg * seglen;
-  const int64_t chunk = (int64_t)tile * kSortTile + (int64_t)warp * 32 * kSortItems;
+  const int64_t tile0 = (int64_t)tile * kSortTile;
+  const int valid_n = (int)min((int64_t)kSortTile, seglen - tile0);
+  const int64_t chunk = tile0 + (int64_t)warp * 32 * kSortItems;
   const uint32_t lt_mask = (1u << lane) - 1u;
   K key[kSortItems];
   uint32_t val[kSortItems];
@@ -189,13 +240,20 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
     loc[r] = base + rank;
   }
   __syncthreads();
-  for (int d = threadIdx.x; d < kRadix; d += kSortThreads) {
-    int64_t run = offs[((int64_t)seg * kRadix + d) * ntiles + tile];
+  // per digit (one per thread): warp prefixes in place, the tile-local start of
+  // the digit, and the global start of this tile's run of it
+  {
+    const int d = threadIdx.x;  // kSortThreads == kRadix
+    uint32_t run = 0;
 #pragma unroll
     for (int w = 0; w < kSortWarps; ++w) {
-      wbase[w][d] = run;
-      run += wcnt[w][d];
+      const uint32_t c = wcnt[w][d];
+      wcnt[w][d] = run;
+      run += c;
     }
+    const uint32_t start = block_excl_scan256(run, warp_tot);
+    dstart[d] = start;
+    gbase[d] = offs[((int64_t)seg * kRadix + d) * ntiles + tile];
   }
   __syncthreads();
 #pragma unroll
@@ -203,10 +261,18 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
     const int64_t idx = chunk + r * 32 + lane;
     if (idx < seglen) {
       const uint32_t dg = (uint32_t)(key[r] >> shift) & 0xFFu;
-      const int64_t pos = wbase[warp][dg] + loc[r];
-      keys_out[pos] = key[r];
-      vals_out[pos] = val[r];
+      const uint32_t p = dstart[dg] + wcnt[warp][dg] + loc[r];
+      skey[p] = key[r];
+      sval[p] = val[r];
     }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < valid_n; i += kSortThreads) {
+    const K k = skey[i];
+    const uint32_t dg = (uint32_t)(k >> shift) & 0xFFu;
+    const int64_t pos = gbase[dg] + (i - (int)dstart[dg]);
+    keys_out[pos] = k;
+    vals_out[pos] = sval[i];
   }
 }
 
@@ -222,6 +288,18 @@ int radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, b
   SINKSLOT_REQUIRE(ntiles <= 0x7fffffff, "radix sort: segment too long");
   const int64_t nh = nseg * kRadix * ntiles;
   if (key_bits < 1) key_bits = 1;
+  {
+    // the dynamic shared-memory limit is a per-device function attribute
+    static bool configured[64] = {};
+    int dev = 0;
+    SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+      SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(radix_scatter_kernel<K>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)scatter_smem<K>()));
+      if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+  }
   K* kin = keys;
   uint32_t* vin = vals;
   K* kout = keys_alt;
@@ -233,7 +311,7 @@ int radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, b
     radix_hist_kernel<K><<<grid, kSortThreads, 0, stream>>>(kin, seglen, (int)ntiles, shift, hist);
     SINKSLOT_CHECK_LAUNCH();
     SINKSLOT_TRY(scan_exclusive_i64(hist, nh, scan_tmp, nullptr, stream));
-    radix_scatter_kernel<K><<<grid, kSortThreads, 0, stream>>>(
+    radix_scatter_kernel<K><<<grid, kSortThreads, scatter_smem<K>(), stream>>>(
         kin, (first && identity_vals) ? nullptr : vin, kout, vout, seglen, (int)ntiles, shift, hist);
     SINKSLOT_CHECK_LAUNCH();
     first = false;

@@ -10,7 +10,7 @@
 //
 // Layout (built once per solve from the CSR side): tile (p, b) = the entries of
 // panel p whose column lies in block b, ordered by the occurrence of their row
-// within the tile and then by row (see occ_key_kernel), padded to a multiple of
+// within the tile and then by row (see tilekey_kernel), padded to a multiple of
 // 32 entries (one warp slab); per entry one uint2 {row within the panel << 16 |
 // column within the block, fp32 lam bits}.  Padding names row R (a dummy row
 // of the panel state) with lam = -inf, so it adds an exact zero and the inner
@@ -139,7 +139,7 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   Carver bw(nullptr, 0);
   const int64_t e = std::max<int64_t>(nnz, 1);
   bw.take<uint32_t>(e);  // row id
-  for (int i = 0; i < 6; ++i) bw.take<uint32_t>(e);  // keys / values of the two sorts
+  for (int i = 0; i < 4; ++i) bw.take<uint32_t>(e);  // keys / values of the sort
   const int64_t nh = radix_hist_elems(1, e);
   bw.take<int64_t>(std::max<int64_t>(nh, ntiles + 2));
   bw.take<int64_t>(scan_tmp_elems(std::max<int64_t>(nh, ntiles + 2)));
@@ -188,36 +188,6 @@ __global__ void rowid_kernel(const int32_t* __restrict__ ptr, int64_t nseg,
   if ((threadIdx.x & 31) == 0) atomicMax(longest, best);
 }
 
-template <typename IT>
-__global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __restrict__ idx,
-                               int64_t nnz, int R, int B, int logW, uint32_t* __restrict__ key) {
-  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nnz;
-       k += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t r = rowid[k];
-    const uint32_t c = (uint32_t)idx[k];
-    key[k] = (r / (uint32_t)R) * (uint32_t)B + (c >> logW);
-  }
-}
-
-// ustart[t] = #{sorted keys < t}; cntp[t] = entries of tile t rounded up to a slab
-__global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
-                                   int64_t* __restrict__ ustart, int64_t* __restrict__ cntp) {
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t <= ntiles;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    auto lb = [&](int64_t v) {
-      int64_t lo = 0, hi = nnz;
-      while (lo < hi) {
-        const int64_t mid = (lo + hi) >> 1;
-        if ((int64_t)skey[mid] < v) lo = mid + 1; else hi = mid;
-      }
-      return lo;
-    };
-    const int64_t s = lb(t);
-    ustart[t] = s;
-    if (t < ntiles) cntp[t] = (lb(t + 1) - s + kSlab - 1) & ~int64_t(kSlab - 1);
-  }
-}
-
 // Order inside a tile: by the occurrence of the row within the tile (its 1st,
 // 2nd, ... entry there), then by row.  A warp's 32 consecutive entries then
 // name 32 different rows, mostly consecutive ones, so their row-state updates
@@ -227,18 +197,45 @@ __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nn
 constexpr int kOccBits = 6;
 constexpr uint32_t kOccMax = (1u << kOccBits) - 1;
 
-// okey[q] = tile << kOccBits | occurrence of the entry's row within its tile
-// (entries sorted by tile, CSR order inside a tile; occurrences past kOccMax share it)
-__global__ void occ_key_kernel(const uint32_t* __restrict__ skey, const uint32_t* __restrict__ perm,
-                               const uint32_t* __restrict__ rowid, int64_t nnz,
-                               uint32_t* __restrict__ okey) {
-  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
-       q += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t t = skey[q];
-    const uint32_t r = rowid[perm[q]];
-    uint32_t kk = 0;
-    for (int64_t j = q - 1; j >= 0 && kk < kOccMax && skey[j] == t && rowid[perm[j]] == r; --j) ++kk;
-    okey[q] = (t << kOccBits) | kk;
+// key[k] = tile << kOccBits | occurrence of entry k's row within its tile: the
+// number of entries just before k in the same row and the same column block
+// (a row's indices ascend, so its entries of one block are contiguous; past
+// kOccMax they share the last value).  One stable sort by this key gives the
+// layout order.
+template <typename IT>
+__global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __restrict__ idx,
+                               int64_t nnz, int R, int B, int logW, uint32_t* __restrict__ key) {
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nnz;
+       k += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t r = rowid[k];
+    const uint32_t b = (uint32_t)idx[k] >> logW;
+    uint32_t occ = 0;
+    for (int64_t j = k - 1; j >= 0 && occ < kOccMax && rowid[j] == r &&
+                            ((uint32_t)idx[j] >> logW) == b;
+         --j)
+      ++occ;
+    key[k] = (((r / (uint32_t)R) * (uint32_t)B + b) << kOccBits) | occ;
+  }
+}
+
+// ustart[t] = #{sorted keys of tiles < t}; cntp[t] = entries of tile t rounded
+// up to a slab (sorted keys are tile << kOccBits | occurrence)
+__global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
+                                   int64_t* __restrict__ ustart, int64_t* __restrict__ cntp) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t <= ntiles;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    auto lb = [&](int64_t v) {
+      const uint64_t kv = (uint64_t)v << kOccBits;
+      int64_t lo = 0, hi = nnz;
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if ((uint64_t)skey[mid] < kv) lo = mid + 1; else hi = mid;
+      }
+      return lo;
+    };
+    const int64_t s = lb(t);
+    ustart[t] = s;
+    if (t < ntiles) cntp[t] = (lb(t + 1) - s + kSlab - 1) & ~int64_t(kSlab - 1);
   }
 }
 
@@ -250,11 +247,9 @@ __global__ void fill_pad_kernel(uint2* __restrict__ ent, int64_t cap, int R) {
     ent[q] = pad;
 }
 
-// entry q of the final order: okey[q] its (tile, occurrence) key, order[q] its
-// position in the by-tile order, perm[] the CSR entry of that position
+// sorted position q: skey[q] its key, perm[q] its CSR entry
 template <typename IT>
-__global__ void tile_scatter_kernel(const uint32_t* __restrict__ order,
-                                    const uint32_t* __restrict__ okey,
+__global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
                                     const uint32_t* __restrict__ perm,
                                     const uint32_t* __restrict__ rowid, const IT* __restrict__ idx,
                                     const float* __restrict__ lam, int64_t nnz, int R, int logW,
@@ -264,8 +259,8 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ order,
   const uint32_t wmask = (1u << logW) - 1u;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
        q += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t t = okey[q] >> kOccBits;
-    const uint32_t k = perm[order[q]];
+    const uint32_t t = skey[q] >> kOccBits;
+    const uint32_t k = perm[q];
     const int64_t pos = tstart[t] + (q - ustart[t]);
     const uint32_t r = rowid[k];
     const uint32_t c = (uint32_t)idx[k];
@@ -289,8 +284,6 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   uint32_t* v1 = cv.take<uint32_t>(e);
   uint32_t* k2 = cv.take<uint32_t>(e);
   uint32_t* v2 = cv.take<uint32_t>(e);
-  uint32_t* k3 = cv.take<uint32_t>(e);
-  uint32_t* v3 = cv.take<uint32_t>(e);
   const int64_t nh = std::max<int64_t>(radix_hist_elems(1, e), ntiles + 2);
   int64_t* hist = cv.take<int64_t>(nh);
   int64_t* stmp = cv.take<int64_t>(scan_tmp_elems(nh));
@@ -317,9 +310,9 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
         rowid, static_cast<const int32_t*>(idx), g.nnz, g.R, g.B, g.logW, k1);
   SINKSLOT_CHECK_LAUNCH();
   bool alt = false;
-  SINKSLOT_TRY(radix_sort_pairs<uint32_t>(k1, v1, k2, v2, true, 1, g.nnz,
-                                          bits_for((uint64_t)std::max<int64_t>(ntiles, 2)), hist,
-                                          stmp, &alt, st));
+  SINKSLOT_TRY(radix_sort_pairs<uint32_t>(
+      k1, v1, k2, v2, true, 1, g.nnz,
+      bits_for((uint64_t)std::max<int64_t>(ntiles, 2)) + kOccBits, hist, stmp, &alt, st));
   const uint32_t* skey = alt ? k2 : k1;
   const uint32_t* perm = alt ? v2 : v1;
   // padded tile starts: exclusive scan of the rounded-up counts (in L.tstart)
@@ -327,25 +320,14 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
                                                               L.tstart);
   SINKSLOT_CHECK_LAUNCH();
   SINKSLOT_TRY(scan_exclusive_i64(L.tstart, ntiles, stmp, L.tstart + ntiles, st));
-  // second stable sort: by (tile, occurrence of the row in the tile)
-  uint32_t* okey = alt ? k1 : k2;  // the pair the first sort left free
-  uint32_t* oval = alt ? v1 : v2;
-  occ_key_kernel<<<grid_t(g.nnz, 256), 256, 0, st>>>(skey, perm, rowid, g.nnz, okey);
-  SINKSLOT_CHECK_LAUNCH();
-  bool alt2 = false;
-  SINKSLOT_TRY(radix_sort_pairs<uint32_t>(
-      okey, oval, k3, v3, true, 1, g.nnz,
-      bits_for((uint64_t)std::max<int64_t>(ntiles, 2)) + kOccBits, hist, stmp, &alt2, st));
-  const uint32_t* okey_s = alt2 ? k3 : okey;
-  const uint32_t* order = alt2 ? v3 : oval;
   if (idx_bytes == 2)
     tile_scatter_kernel<int16_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-        order, okey_s, perm, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW,
-        ustart, L.tstart, L.ent);
+        skey, perm, rowid, static_cast<const int16_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
+        L.tstart, L.ent);
   else
     tile_scatter_kernel<int32_t><<<grid_t(g.nnz, 256), 256, 0, st>>>(
-        order, okey_s, perm, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW,
-        ustart, L.tstart, L.ent);
+        skey, perm, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
+        L.tstart, L.ent);
   SINKSLOT_CHECK_LAUNCH();
   return kOk;
 }
