@@ -638,7 +638,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     // Tile b holds slabs [e0, e1) / 32 of the layout.  Warp w takes groups of
     // kGroup consecutive slabs starting at kGroup*w, kGroup*(w + warps), ...; its first group of
     // the next tile is loaded while the current tile is processed.
+    // tile starts: e0, e1 bound tile b, f1n the end of tile b + 1 (loaded a
+    // tile ahead of its use, so no tile waits on a global load of its bounds)
     int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
+    int64_t f1n = a.B > 1 ? a.tstart[pb + 2] : e1;
     uint2 en[kGroup];
     load_group(a.ent, e0, (int)((e1 - e0) / kSlab), kGroup * warp, lane, en);
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
@@ -648,7 +651,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
 #pragma unroll
       for (int j = 0; j < kGroup; ++j) e[j] = en[j];
       const int64_t f0 = e1;
-      const int64_t f1 = b + 1 < a.B ? a.tstart[pb + b + 2] : e1;
+      const int64_t f1 = b + 1 < a.B ? f1n : e1;
+      if (b + 2 < a.B) f1n = a.tstart[pb + b + 3];
       load_group(a.ent, f0, (int)((f1 - f0) / kSlab), kGroup * warp, lane, en);
       const int s = sb;
       if (!(ok = warp_wait(pot_full(s), ub, abort_w, a.err, 3))) break;
