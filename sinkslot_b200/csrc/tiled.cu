@@ -37,10 +37,11 @@
 // are summed with native 32-bit shared-memory integer atomics -- exact and
 // order-independent, so the result is deterministic.  The high-part sum cannot
 // overflow because terms are capped at 2^k with k = 20 - ceil(log2(longest
-// row)); the low-part sum cannot overflow for rows of up to 4096 entries.  A
-// row is handed back to the exact (max-stabilised) kernel when a term exceeds
-// the cap or its sum is below 2^-8 -- the first iteration, where sigma is not
-// yet an estimate, and any row whose potential moved by more than a few units.
+// row)); the low-part sum cannot overflow for rows of up to 4096 entries, and
+// longer rows are handed back to the exact (max-stabilised) kernel whole.  A
+// row is also handed back when a term exceeds the cap or its sum is below 2^-8
+// -- the first iteration, where sigma is not yet an estimate, and any row whose
+// potential moved by more than a few units.
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -81,6 +82,9 @@ constexpr float kFixScale = 4294967296.0f;  // 2^32
 constexpr double kFixInv = 1.0 / 4294967296.0;
 constexpr unsigned long long kFixMin = 1ull << 24;  // sums below 2^-8 go to the exact pass
 constexpr int kLoBits = 20;
+// rows up to this length are summed by the tiled pass (their low-part sum of
+// terms below 2^20 stays below 2^32); longer rows always go to the exact pass
+constexpr int64_t kMaxTiledRow = 4096;
 constexpr long long kWaitCycles = 8000000000ll;  // ~4 s at 2 GHz: a wait this long is a bug
 
 constexpr int kSlab = 32;  // tiles are padded to whole warp slabs of entries
@@ -132,7 +136,7 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   const int64_t ntiles = (int64_t)g.P * g.B;
   g.cap = nnz + (kSlab - 1) * ntiles;
   Carver cv(nullptr, 0);
-  cv.take<int64_t>(8);            // header: [0] longest row
+  cv.take<int64_t>(8);            // header: [0] longest row of <= kMaxTiledRow entries
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
   cv.take<uint2>(std::max<int64_t>(g.cap, 1));  // entries {meta, lam bits}
   g.layout_bytes = cv.used;
@@ -179,7 +183,9 @@ __global__ void rowid_kernel(const int32_t* __restrict__ ptr, int64_t nseg,
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t s = ptr[i], e = ptr[i + 1];
     for (int64_t k = s; k < e; ++k) rowid[k] = (uint32_t)i;
-    if ((unsigned long long)(e - s) > best) best = (unsigned long long)(e - s);
+    // the longest row the tiled pass sums (longer ones are handed back whole)
+    if (e - s <= kMaxTiledRow && (unsigned long long)(e - s) > best)
+      best = (unsigned long long)(e - s);
   }
   for (int o = 16; o >= 1; o >>= 1) {
     const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
@@ -432,6 +438,7 @@ struct TKArgs {
   const int64_t* header;
   const int64_t* tstart;
   const uint2* ent;
+  const int32_t* ptr;  // the CSR offsets (row lengths)
   const float* other;
   const float* base;
   const float* self_old;
@@ -615,7 +622,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   while ((1ll << lg) < longest) ++lg;
   const int k = kLoBits - lg;
   // terms above 2^k would overflow the high-part sum of the longest row
-  const float capd = (longest <= 4096 && k >= 1) ? ((float)k - 0.01f) * 0.69314718f : -INFINITY;
+  const float capd = (longest <= kMaxTiledRow && k >= 1) ? ((float)k - 0.01f) * 0.69314718f
+                                                         : -INFINITY;
   uint32_t chk_bits = 0;
   int sb = 0;
   uint32_t ub = 0;
@@ -627,14 +635,25 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     const int rows = (int)std::min<int64_t>(a.R, a.nseg - row0);
     if (rows <= 0) break;
     const int64_t pb = (int64_t)p * a.B;
-    for (int r = tid; r <= a.R; r += kConsumers) {
-      uint32_t* st = row_state(smem, (uint32_t)r);
-      st[0] = __float_as_uint(
-          r < rows ? __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]) : 0.0f);
-      st[1] = 0u;
-      st[2] = 0u;
+    // row state (warp w initialises rows 32w .. 32w+31, then 32(w+31) ...) and
+    // flag words: rows longer than kMaxTiledRow are handed back from the start
+    for (int r0 = warp * 32; r0 <= a.R; r0 += kConsumers) {
+      const int r = r0 + lane;
+      bool longrow = false;
+      if (r <= a.R) {
+        uint32_t* st = row_state(smem, (uint32_t)r);
+        float sg = 0.0f;
+        if (r < rows) {
+          sg = __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
+          longrow = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
+        }
+        st[0] = __float_as_uint(sg);
+        st[1] = 0u;
+        st[2] = 0u;
+      }
+      const uint32_t word = __ballot_sync(0xffffffffu, longrow);
+      if (lane == 0) flags[r0 >> 5] = word;
     }
-    for (int r = tid; r < (a.R + 1 + 31) / 32; r += kConsumers) flags[r] = 0u;
     // Tile b holds slabs [e0, e1) / 32 of the layout.  Warp w takes groups of
     // kGroup consecutive slabs starting at kGroup*w, kGroup*(w + warps), ...; its first group of
     // the next tile is loaded while the current tile is processed.
@@ -730,6 +749,7 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.header = L.header;
   a.tstart = L.tstart;
   a.ent = L.ent;
+  a.ptr = h.ptr;
   a.other = h.other;
   a.base = h.base;
   a.self_old = h.self_old;

@@ -109,6 +109,7 @@ CASES = [
     (60000, 60000, 3, "uniform", 0.01, 64),
     (20000, 30000, 2, "dirichlet", 0.002, 48),   # small eps: rows handed back
     (3000, 3000, 4, "dirichlet", 2.0, 16),       # large eps
+    (100, 50000, 2, "dirichlet", 0.05, 16),      # rows of > 4096 entries: handed back whole
 ]
 
 
