@@ -28,14 +28,18 @@ namespace sinkslot {
 constexpr int kLseThreads = 256;
 constexpr int kLseUnroll = 4;
 
+// One half-step over the segments of a CSR side, by the whole grid: G lanes
+// per segment, online max / sum, then the epilogue; the check maxima go to acc.
 template <typename IT, int G, int OUT, int CHK>
-__global__ void __launch_bounds__(kLseThreads) half_step_kernel(
-    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, const float* __restrict__ lam,
-    const float* __restrict__ other, const float* __restrict__ selfpot,
-    const float* __restrict__ base,
-    const float* self_old, float* out, int64_t nseg, float w_old, float w_new, float* prev,
-    uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count,
-    const PeerOut po, unsigned int* done) {
+__device__ __forceinline__ void seg_pass(const int32_t* __restrict__ ptr,
+                                         const IT* __restrict__ idx,
+                                         const float* __restrict__ lam,
+                                         const float* __restrict__ other,
+                                         const float* __restrict__ selfpot,
+                                         const float* __restrict__ base, const float* self_old,
+                                         float* out, int64_t nseg, float w_old, float w_new,
+                                         float* prev, uint32_t* acc, const int* __restrict__ list,
+                                         const int* __restrict__ list_count, const PeerOut& po) {
   // self_old and out alias in the Gauss-Seidel variant (in-place update): no
   // __restrict__ on either, so the old value is read before the store.
   // With `list`, only the segments list[0 .. *list_count) are computed (the rows
@@ -102,6 +106,18 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     }
   }
   check_reduce<CHK>(chk_bits, acc);
+}
+
+template <typename IT, int G, int OUT, int CHK>
+__global__ void __launch_bounds__(kLseThreads) half_step_kernel(
+    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, const float* __restrict__ lam,
+    const float* __restrict__ other, const float* __restrict__ selfpot,
+    const float* __restrict__ base,
+    const float* self_old, float* out, int64_t nseg, float w_old, float w_new, float* prev,
+    uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count,
+    const PeerOut po, unsigned int* done) {
+  seg_pass<IT, G, OUT, CHK>(ptr, idx, lam, other, selfpot, base, self_old, out, nseg, w_old,
+                            w_new, prev, acc, list, list_count, po);
   if (po.n > 0) {
     __syncthreads();
     peer_cta_done(po, done);
