@@ -6,8 +6,9 @@
 //   project_keys_kernel    PX = X @ theta^T as the sequential fp32 FMA chain over d
 //                          (what cuBLAS computes for K = d), written as radix keys
 //   radix_sort_pairs       per-slice stable argsort (CUB semantics: stable, -0 == +0)
-//   slice_cumsum_kernel    cumsum(a[ix]) in torch's CUDA innermost-dim scan order
-//                          (Sklansky chunks, ATen/native/cuda/ScanUtils.cuh)
+//   chunk_*_kernel         cumsum(a[ix]) in torch's CUDA innermost-dim scan order
+//                          (Sklansky chunks, ATen/native/cuda/ScanUtils.cuh),
+//                          chunks in parallel around a per-row carry chain
 //   merge_count/emit       rank merge of the two cumsums + midpoint searchsorted,
 //                          as one merge-path walk (replaces 4 searchsorted + 2 scatters)
 //   radix_sort_pairs<u64>  stable sort of raw keys r*m+c
@@ -122,44 +123,77 @@ uint32_t torch_inner_scan_log_tx(uint32_t num_rows, uint32_t row_size) {
   return lx;
 }
 
-__global__ void slice_cumsum_kernel(const uint32_t* __restrict__ order, const float* __restrict__ w,
-                                    float* __restrict__ out, int64_t len, int C, int log_tx) {
-  extern __shared__ float sbuf[];
-  const int tx = 1 << log_tx;
-  float* row_buf = sbuf + 2 * tx * threadIdx.y;
-  for (int64_t block_row = (int64_t)blockIdx.x * blockDim.y; block_row < C;
-       block_row += (int64_t)blockDim.y * gridDim.x) {
-    const int64_t row = block_row + threadIdx.y;
-    const bool exists = row < C;
-    const uint32_t* ord = order + row * len;
-    float* dst = out + row * len;
-    float total = 0.0f;
-    for (int64_t col = 0; col < len; col += 2 * tx) {
-      const int64_t c1 = col + threadIdx.x, c2 = col + tx + threadIdx.x;
-      if (exists) {
-        row_buf[threadIdx.x] = c1 < len ? __ldg(w + ord[c1]) : 0.0f;
-        row_buf[tx + threadIdx.x] = c2 < len ? __ldg(w + ord[c2]) : 0.0f;
-        if (threadIdx.x == 0) row_buf[0] = __fadd_rn(row_buf[0], total);
-      }
-      __syncthreads();
-      for (int mm = 0; mm <= log_tx; ++mm) {
-        if (exists) {
-          const uint32_t s = 1u << mm;
-          const uint32_t a = ((threadIdx.x >> mm) << (mm + 1)) | s;
-          const uint32_t ti = a + (threadIdx.x % s);
-          const uint32_t si = a - 1;
-          row_buf[ti] = __fadd_rn(row_buf[ti], row_buf[si]);
-        }
-        __syncthreads();
-      }
-      if (exists) {
-        if (c1 < len) dst[c1] = row_buf[threadIdx.x];
-        if (c2 < len) dst[c2] = row_buf[tx + threadIdx.x];
-      }
-      total = row_buf[2 * tx - 1];
-      __syncthreads();
-    }
+// The same scan in three parallel steps with the same fp32 operations.  In a
+// chunk of 2*tx elements the carry enters at element 0 (x0 + carry) and reaches
+// the chunk's last element through one add per Sklansky level j = 1..L
+// (L = log_tx + 1): T_j = R_j + T_{j-1}, where R_j, the tree total of block
+// [2^(j-1), 2^j) after levels 0..j-2, does not depend on the carry.  So:
+//   1. chunk_parts_kernel: per chunk, x0 and R_1..R_L (all chunks in parallel);
+//   2. chunk_carry_kernel: per row, the chain of carries (L + 1 adds per chunk);
+//   3. chunk_scan_kernel: per chunk, the full scan with x0 + its carry.
+__global__ void chunk_parts_kernel(const uint32_t* __restrict__ order, const float* __restrict__ w,
+                                   int64_t len, int log_tx, int64_t nchunks,
+                                   float* __restrict__ parts) {
+  extern __shared__ float buf[];
+  const int tx = 1 << log_tx, L = log_tx + 1;
+  const int t = threadIdx.x;
+  const int64_t row = blockIdx.y, chunk = blockIdx.x;
+  const uint32_t* ord = order + row * len;
+  const int64_t c1 = chunk * 2 * tx + t, c2 = c1 + tx;
+  buf[t] = c1 < len ? __ldg(w + ord[c1]) : 0.0f;
+  buf[tx + t] = c2 < len ? __ldg(w + ord[c2]) : 0.0f;
+  float* P = parts + (row * nchunks + chunk) * (L + 1);
+  if (t == 0) P[0] = buf[0];
+  __syncthreads();
+  for (int mm = 0; mm <= log_tx; ++mm) {
+    const uint32_t sz = 1u << mm;
+    const uint32_t a = ((t >> mm) << (mm + 1)) | sz;
+    const uint32_t ti = a + (t % sz);
+    const uint32_t si = a - 1;
+    if (ti == 2 * sz - 1) P[mm + 1] = buf[ti];  // R_{mm+1}, before this level adds to it
+    buf[ti] = __fadd_rn(buf[ti], buf[si]);
+    __syncthreads();
   }
+}
+
+__global__ void chunk_carry_kernel(const float* __restrict__ parts, int C, int64_t nchunks,
+                                   int L, float* __restrict__ carry) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= C) return;
+  float c = 0.0f;
+  for (int64_t k = 0; k < nchunks; ++k) {
+    const float* P = parts + ((int64_t)row * nchunks + k) * (L + 1);
+    carry[(int64_t)row * nchunks + k] = c;
+    float T = __fadd_rn(P[0], c);
+    for (int j = 1; j <= L; ++j) T = __fadd_rn(P[j], T);
+    c = T;
+  }
+}
+
+__global__ void chunk_scan_kernel(const uint32_t* __restrict__ order, const float* __restrict__ w,
+                                  float* __restrict__ out, int64_t len, int log_tx,
+                                  int64_t nchunks, const float* __restrict__ carry) {
+  extern __shared__ float buf[];
+  const int tx = 1 << log_tx;
+  const int t = threadIdx.x;
+  const int64_t row = blockIdx.y, chunk = blockIdx.x;
+  const uint32_t* ord = order + row * len;
+  float* dst = out + row * len;
+  const int64_t c1 = chunk * 2 * tx + t, c2 = c1 + tx;
+  buf[t] = c1 < len ? __ldg(w + ord[c1]) : 0.0f;
+  buf[tx + t] = c2 < len ? __ldg(w + ord[c2]) : 0.0f;
+  if (t == 0) buf[0] = __fadd_rn(buf[0], carry[row * nchunks + chunk]);
+  __syncthreads();
+  for (int mm = 0; mm <= log_tx; ++mm) {
+    const uint32_t sz = 1u << mm;
+    const uint32_t a = ((t >> mm) << (mm + 1)) | sz;
+    const uint32_t ti = a + (t % sz);
+    const uint32_t si = a - 1;
+    buf[ti] = __fadd_rn(buf[ti], buf[si]);
+    __syncthreads();
+  }
+  if (c1 < len) dst[c1] = buf[t];
+  if (c2 < len) dst[c2] = buf[tx + t];
 }
 
 // Sequential fp32 scan.  With C == 1 torch scans a 1-D tensor with CUB's
@@ -176,8 +210,11 @@ __global__ void slice_cumsum_seq_kernel(const uint32_t* __restrict__ order,
   }
 }
 
+// torch's scan order for C rows of len (C > 1): chunks of 2*tx elements, tx from
+// torch_inner_scan_log_tx.  `scratch`: C * nchunks * (log_tx + 3) floats, less
+// than C * len since 2 * tx >= 32.
 static int slice_cumsum(const uint32_t* order, const float* w, float* out, int64_t len, int C,
-                        cudaStream_t stream) {
+                        float* scratch, cudaStream_t stream) {
   if (len == 0 || C == 0) return kOk;
   if (C == 1) {
     slice_cumsum_seq_kernel<<<1, 32, 0, stream>>>(order, w, out, len);
@@ -185,10 +222,20 @@ static int slice_cumsum(const uint32_t* order, const float* w, float* out, int64
     return kOk;
   }
   const int log_tx = (int)torch_inner_scan_log_tx((uint32_t)C, (uint32_t)len);
-  const int tx = 1 << log_tx, ty = 512 / tx;
-  const unsigned grid = (unsigned)ceil_div64(C, ty);
-  slice_cumsum_kernel<<<grid, dim3(tx, ty), 512 * 2 * sizeof(float), stream>>>(order, w, out, len,
-                                                                                C, log_tx);
+  const int tx = 1 << log_tx;
+  const int64_t nchunks = ceil_div64(len, (int64_t)2 * tx);
+  SINKSLOT_REQUIRE(nchunks <= 0x7fffffff && C <= 65535, "cumsum: too many chunks or rows");
+  float* parts = scratch;
+  float* carry = scratch + (int64_t)C * nchunks * (log_tx + 2);
+  const dim3 grid((unsigned)nchunks, (unsigned)C);
+  chunk_parts_kernel<<<grid, tx, 2 * tx * sizeof(float), stream>>>(order, w, len, log_tx, nchunks,
+                                                                    parts);
+  SINKSLOT_CHECK_LAUNCH();
+  chunk_carry_kernel<<<(unsigned)ceil_div64(C, 64), 64, 0, stream>>>(parts, C, nchunks,
+                                                                      log_tx + 1, carry);
+  SINKSLOT_CHECK_LAUNCH();
+  chunk_scan_kernel<<<grid, tx, 2 * tx * sizeof(float), stream>>>(order, w, out, len, log_tx,
+                                                                   nchunks, carry);
   SINKSLOT_CHECK_LAUNCH();
   return kOk;
 }
@@ -434,8 +481,9 @@ static int slices_prepare(SliceBufs& b, const float* a, const float* bw, int64_t
   SINKSLOT_TRY(radix_sort_pairs<uint32_t>(b.ky, b.vy, b.ky2, b.vy2, true, C, m, 32, b.hist, b.stmp,
                                           &alt, stream));
   const uint32_t* iy = alt ? b.vy2 : b.vy;
-  SINKSLOT_TRY(slice_cumsum(ix, a, b.ca, n, C, stream));
-  SINKSLOT_TRY(slice_cumsum(iy, bw, b.cb, m, C, stream));
+  // the sort keys are dead once the orders exist: their buffers hold the scan's scratch
+  SINKSLOT_TRY(slice_cumsum(ix, a, b.ca, n, C, reinterpret_cast<float*>(b.kx2), stream));
+  SINKSLOT_TRY(slice_cumsum(iy, bw, b.cb, m, C, reinterpret_cast<float*>(b.ky2), stream));
   const int tps = (int)ceil_div64(n + m, kMergeTile);
   merge_count_kernel<<<dim3(tps, C), kMergeThreads, 0, stream>>>(b.ca, b.cb, n, m, tps, b.counts);
   SINKSLOT_CHECK_LAUNCH();
