@@ -219,3 +219,44 @@ def test_sharded_loop_matches_single_loop(world, variant, mode):
         np.testing.assert_allclose(rpsi, psi, rtol=1e-5, atol=1e-5)
         if mode != "fixed":
             assert rviol == pytest.approx(viol, rel=1e-3, abs=1e-9)
+
+
+def _dying_rank_main(rank, world, port, q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    try:
+        def run_chunk(it0, k, check):
+            if rank == 1 and it0 > 0:
+                raise RuntimeError("rank 1 stops between chunks")
+            return 0.5, 0.5
+
+        def reduce_max(a0, a1):
+            t = torch.tensor([a0, a1], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return tuple(t.tolist())
+
+        drive(run_chunk, reduce_max, "marginal", 0, 100, 5, 1e-9, 0.05, 0.5, "alternating")
+        q.put((rank, "finished"))
+    except Exception as e:  # the surviving rank must see an error, not hang
+        q.put((rank, f"error {type(e).__name__}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a_rank_that_leaves_between_chunks_is_an_error_on_the_others():
+    """A rank leaves between chunks (no kernel in flight): the next stop check's
+    reduction fails on the surviving rank with an error instead of waiting."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=90) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1].startswith("error RuntimeError")
+    assert got[0].startswith("error"), got[0]
