@@ -9,9 +9,9 @@
 // shared-memory load.
 //
 // Layout (built once per solve from the CSR side): tile (p, b) = the entries of
-// panel p whose column lies in block b, ordered by the occurrence of their row
-// within the tile and then by row (see tilekey_kernel), padded to a multiple of
-// 32 entries (one warp slab); per entry one uint2 {row within the panel << 16 |
+// panel p whose column lies in block b, padded to a multiple of 32 entries (one
+// warp slab) and arranged so that a slab's rows fall in different shared-memory
+// banks (see tilekey_kernel); per entry one uint2 {row within the panel << 16 |
 // column within the block, fp32 lam bits}.  Padding names row R (a dummy row
 // of the panel state) with lam = -inf, so it adds an exact zero and the inner
 // loop needs no test for it.
@@ -67,6 +67,9 @@ constexpr size_t kSmemCap = 227 * 1024;
 //   SINKSLOT_TILE_ROWS_KB  budget for the per-row state; more panels than SMs
 //                          are used (each SM walks several) to stay within it
 //   SINKSLOT_TILE_MAX_LOGW widest potential block (2^x floats)
+//   SINKSLOT_TILE_PF_LEAD  tiles between the one whose entries the producer
+//                          prefetches into L2 and the one whose block it copies
+//   SINKSLOT_TILE_PF_BYTES largest single L2 prefetch (a tile's range is split)
 #ifndef SINKSLOT_TILE_STAGES
 #define SINKSLOT_TILE_STAGES 2
 #endif
@@ -76,7 +79,16 @@ constexpr size_t kSmemCap = 227 * 1024;
 #ifndef SINKSLOT_TILE_MAX_LOGW
 #define SINKSLOT_TILE_MAX_LOGW 14
 #endif
+#ifndef SINKSLOT_TILE_PF_LEAD
+#define SINKSLOT_TILE_PF_LEAD 0
+#endif
+#ifndef SINKSLOT_TILE_PF_BYTES
+#define SINKSLOT_TILE_PF_BYTES (1 << 30)
+#endif
 constexpr int kStages = SINKSLOT_TILE_STAGES;
+constexpr int kPfLead = SINKSLOT_TILE_PF_LEAD;
+constexpr uint32_t kPfBytes = SINKSLOT_TILE_PF_BYTES;
+static_assert(kPfLead >= 0 && kPfBytes >= 256 && kPfBytes % 256 == 0, "prefetch tuning");
 constexpr size_t kBarBytes = align_up(16 * kStages + 16, 128);  // 2 mbarriers per stage + abort
 constexpr float kFixScale = 4294967296.0f;  // 2^32
 constexpr double kFixInv = 1.0 / 4294967296.0;
@@ -194,20 +206,22 @@ __global__ void rowid_kernel(const int32_t* __restrict__ ptr, int64_t nseg,
   if ((threadIdx.x & 31) == 0) atomicMax(longest, best);
 }
 
-// Order inside a tile: by the occurrence of the row within the tile (its 1st,
-// 2nd, ... entry there), then by row.  A warp's 32 consecutive entries then
-// name 32 different rows, mostly consecutive ones, so their row-state updates
-// do not collide in shared memory (CSR order would put a row's entries side by
-// side: same address in neighbouring lanes).  The sums are exact fixed point,
-// so the order does not change any result.
-constexpr int kOccBits = 6;
-constexpr uint32_t kOccMax = (1u << kOccBits) - 1;
+// Order inside a tile.  A warp slab (32 consecutive entries) reads and updates
+// the state of its 32 rows in shared memory; row r's three words sit in banks
+// (3r + j) mod 32, so two rows of a slab share a bank exactly when their
+// panel-local indices agree mod 32.  The tile's entries are sorted by that
+// residue (its "bank"), then dealt across the tile's N slabs with stride N:
+// sorted position p goes to slab p mod N, lane p / N.  A bank's run of c
+// consecutive sorted positions lands in min(c, N) different slabs, so a slab
+// holds at most ceil(c / N) rows of any bank -- one, unless that bank has more
+// than N entries in the tile -- and 32 different rows.  Row order (consecutive
+// rows in neighbouring lanes) would leave two-way conflicts in most slabs, the
+// warp spanning more than 32 row indices once rows skip.  The sums are exact
+// fixed point, so the order does not change any result.
+constexpr int kBankBits = 5;
 
-// key[k] = tile << kOccBits | occurrence of entry k's row within its tile: the
-// number of entries just before k in the same row and the same column block
-// (a row's indices ascend, so its entries of one block are contiguous; past
-// kOccMax they share the last value).  One stable sort by this key gives the
-// layout order.
+// key[k] = tile << kBankBits | bank of entry k's row.  One stable sort by this
+// key gives the tile runs, each ordered by bank.
 template <typename IT>
 __global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __restrict__ idx,
                                int64_t nnz, int R, int B, int logW, uint32_t* __restrict__ key) {
@@ -215,23 +229,20 @@ __global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __r
        k += (int64_t)gridDim.x * blockDim.x) {
     const uint32_t r = rowid[k];
     const uint32_t b = (uint32_t)idx[k] >> logW;
-    uint32_t occ = 0;
-    for (int64_t j = k - 1; j >= 0 && occ < kOccMax && rowid[j] == r &&
-                            ((uint32_t)idx[j] >> logW) == b;
-         --j)
-      ++occ;
-    key[k] = (((r / (uint32_t)R) * (uint32_t)B + b) << kOccBits) | occ;
+    const uint32_t pnl = r / (uint32_t)R;
+    const uint32_t bank = (r - pnl * (uint32_t)R) & ((1u << kBankBits) - 1u);
+    key[k] = ((pnl * (uint32_t)B + b) << kBankBits) | bank;
   }
 }
 
 // ustart[t] = #{sorted keys of tiles < t}; cntp[t] = entries of tile t rounded
-// up to a slab (sorted keys are tile << kOccBits | occurrence)
+// up to a slab (sorted keys are tile << kBankBits | bank)
 __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
                                    int64_t* __restrict__ ustart, int64_t* __restrict__ cntp) {
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t <= ntiles;
        t += (int64_t)gridDim.x * blockDim.x) {
     auto lb = [&](int64_t v) {
-      const uint64_t kv = (uint64_t)v << kOccBits;
+      const uint64_t kv = (uint64_t)v << kBankBits;
       int64_t lo = 0, hi = nnz;
       while (lo < hi) {
         const int64_t mid = (lo + hi) >> 1;
@@ -253,7 +264,8 @@ __global__ void fill_pad_kernel(uint2* __restrict__ ent, int64_t cap, int R) {
     ent[q] = pad;
 }
 
-// sorted position q: skey[q] its key, perm[q] its CSR entry
+// sorted position q: skey[q] its key, perm[q] its CSR entry; its position p in
+// its tile's sorted run goes to slab p mod N, lane p / N of the tile's N slabs
 template <typename IT>
 __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
                                     const uint32_t* __restrict__ perm,
@@ -265,9 +277,13 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
   const uint32_t wmask = (1u << logW) - 1u;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
        q += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t t = skey[q] >> kOccBits;
+    const uint32_t t = skey[q] >> kBankBits;
     const uint32_t k = perm[q];
-    const int64_t pos = tstart[t] + (q - ustart[t]);
+    const int64_t ts = tstart[t];
+    const uint32_t ns = (uint32_t)((tstart[t + 1] - ts) >> 5);  // slabs of the tile (>= 1)
+    const uint32_t p = (uint32_t)(q - ustart[t]);               // nnz < 2^32
+    const uint32_t lane = p / ns;
+    const int64_t pos = ts + ((int64_t)(p - lane * ns) << 5) + lane;
     const uint32_t r = rowid[k];
     const uint32_t c = (uint32_t)idx[k];
     ent[pos] = make_uint2(((r % (uint32_t)R) << 16) | (c & wmask), __float_as_uint(lam[k]));
@@ -279,7 +295,7 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   SINKSLOT_REQUIRE(idx_bytes == 2 || idx_bytes == 4, "build_tiles: idx_bytes must be 2 or 4");
   SINKSLOT_REQUIRE(g.nnz < (int64_t(1) << 32), "build_tiles: nnz must be < 2^32");
   SINKSLOT_REQUIRE(g.P > 0 && g.B > 0, "build_tiles: empty geometry");
-  SINKSLOT_REQUIRE((int64_t)g.P * g.B < (int64_t(1) << (32 - kOccBits)),
+  SINKSLOT_REQUIRE((int64_t)g.P * g.B < (int64_t(1) << (32 - kBankBits)),
                    "build_tiles: too many tiles");
   LayoutPtrs L = carve_layout(layout, g);
   Carver cv(ws, ws_bytes);
@@ -318,7 +334,7 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   bool alt = false;
   SINKSLOT_TRY(radix_sort_pairs<uint32_t>(
       k1, v1, k2, v2, true, 1, g.nnz,
-      bits_for((uint64_t)std::max<int64_t>(ntiles, 2)) + kOccBits, hist, stmp, &alt, st));
+      bits_for((uint64_t)std::max<int64_t>(ntiles, 2)) + kBankBits, hist, stmp, &alt, st));
   const uint32_t* skey = alt ? k2 : k1;
   const uint32_t* perm = alt ? v2 : v1;
   // padded tile starts: exclusive scan of the rounded-up counts (in L.tstart)
@@ -496,6 +512,19 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Entries [e0, e1) of the layout into L2, in prefetches of at most kPfBytes
+// (tile ranges start on 256-byte boundaries and span whole 256-byte slabs).
+__device__ __forceinline__ void prefetch_entries(const uint2* ent, int64_t e0, int64_t e1) {
+  const char* p = reinterpret_cast<const char*>(ent + e0);
+  int64_t left = (e1 - e0) * (int64_t)sizeof(uint2);
+  while (left > 0) {
+    const uint32_t n = left < (int64_t)kPfBytes ? (uint32_t)left : kPfBytes;
+    prefetch_l2(p, n);
+    p += n;
+    left -= n;
+  }
+}
+
 // Lane `lane` of slabs g .. g+kGroup-1 of the tile whose entries start at e0
 // (only the slabs below nsl are loaded): coalesced 8-byte streaming loads, 256
 // bytes per slab.
@@ -583,13 +612,19 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     for (int p = blockIdx.x; ok && p < a.P; p += gridDim.x) {
       if ((int64_t)p * a.R >= a.nseg) break;
       const int64_t pb = (int64_t)p * a.B;
-      int64_t e0 = a.tstart[pb], e1n = a.tstart[pb + 1];
+      // entries of tiles [0, kPfLead) into L2 now; then, with block b, those of
+      // tile b + kPfLead (pf0 .. pf1; the end after it is loaded a tile early)
+      int64_t pf0 = a.tstart[pb + (kPfLead < a.B ? kPfLead : a.B)];
+      if (kPfLead > 0) prefetch_entries(a.ent, a.tstart[pb], pf0);
+      int64_t pf1 = kPfLead < a.B ? a.tstart[pb + kPfLead + 1] : pf0;
       for (int b = 0; ok && b < a.B; ++b) {
-        const int64_t e1 = e1n;
-        // next tile's end: loaded now, used after this tile's waits
-        if (b + 1 < a.B) e1n = a.tstart[pb + b + 2];
-        // the tile's entries into L2 ahead of the consumers' loads
-        if (e1 > e0) prefetch_l2(a.ent + e0, (uint32_t)((e1 - e0) * sizeof(uint2)));
+        if (b + kPfLead < a.B) {
+          const int64_t s0 = pf0, s1 = pf1;
+          pf0 = pf1;
+          if (b + kPfLead + 2 <= a.B) pf1 = a.tstart[pb + b + kPfLead + 2];
+          // tile b + kPfLead's entries into L2 ahead of the consumers' loads
+          prefetch_entries(a.ent, s0, s1);
+        }
         if (nb >= kStages && !(ok = mbar_wait(pot_empty(sb), ub ^ 1u, abort_w, a.err, 1))) break;
         const int64_t c0 = (int64_t)b * W;
         const int64_t cnt = std::min<int64_t>(W, a.m_o - c0);
@@ -601,7 +636,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
         if (body > 0) bulk_g2s(smem_u32(dst), a.other + c0, (uint32_t)(body * 4), pot_full(sb));
         ++nb;
         if (++sb == kStages) { sb = 0; ub ^= 1u; }
-        e0 = e1;
       }
     }
     if (!ok) {

@@ -11,9 +11,9 @@ namespace sinkslot {
 
 // Geometry of a tiled layout: P panels of R rows; the gathered axis (length
 // m_o) cut into B blocks of W = 2^logW entries.  Tile (p, b) holds the entries
-// of panel p whose column falls in block b (ordered by the occurrence of their
-// row within the tile, then by row), padded to a multiple of 32 entries (warp
-// slabs).
+// of panel p whose column falls in block b, padded to a multiple of 32 entries
+// (warp slabs) and dealt so that a slab's rows lie in different shared-memory
+// banks.
 struct TileGeom {
   int64_t nseg = 0, m_o = 0, nnz = 0;
   int P = 0, R = 0, B = 0, logW = 0;

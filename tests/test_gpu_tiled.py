@@ -81,14 +81,8 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     lam_h = lam.cpu().numpy()
     row_of = np.repeat(np.arange(n), np.diff(ptr_h))
     tile_of = (row_of // R) * B + (idx_h >> logW)
-    by_tile = np.argsort(tile_of, kind="stable")
-    # inside a tile: by the occurrence of the row there (capped at 63), then by row
-    t_s, r_s = tile_of[by_tile], row_of[by_tile]
-    occ = np.zeros(nnz, dtype=np.int64)
-    for q in range(1, nnz):
-        if t_s[q] == t_s[q - 1] and r_s[q] == r_s[q - 1]:
-            occ[q] = occ[q - 1] + 1
-    order = by_tile[np.lexsort((np.arange(nnz), np.minimum(occ, 63), t_s))]
+    # inside a tile: stably by the bank of the row state, (row within panel) mod 32
+    order = np.lexsort((np.arange(nnz), (row_of % R) % 32, tile_of))
     counts = np.bincount(tile_of, minlength=T)
     padded = (counts + 31) // 32 * 32
     np.testing.assert_array_equal(tstart, np.concatenate([[0], np.cumsum(padded)]))
@@ -96,7 +90,11 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     want_meta = np.full(cap, R << 16, dtype=np.uint64)
     want_lam = np.full(cap, -np.inf, dtype=np.float32)
     ustart = np.concatenate([[0], np.cumsum(counts)])
-    pos = tstart[tile_of[order]] + (np.arange(nnz) - ustart[tile_of[order]])
+    t_o = tile_of[order]
+    p = np.arange(nnz) - ustart[t_o]
+    ns = padded[t_o] // 32
+    # sorted position p of a tile with N slabs: slab p mod N, lane p // N
+    pos = tstart[t_o] + 32 * (p % ns) + p // ns
     want_meta[pos] = ((row_of[order] % R) << 16) | (idx_h[order] & ((1 << logW) - 1))
     want_lam[pos] = lam_h[order]
     np.testing.assert_array_equal(meta, want_meta.astype(np.uint32))
