@@ -689,10 +689,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       if (lane == 0) flags[r0 >> 5] = word;
     }
     // Tile b holds slabs [e0, e1) / 32 of the layout.  Warp w takes groups of
-    // kGroup consecutive slabs starting at kGroup*w, kGroup*(w + warps), ...; its first group of
-    // the next tile is loaded while the current tile is processed.
-    // tile starts: e0, e1 bound tile b, f1n the end of tile b + 1 (loaded a
-    // tile ahead of its use, so no tile waits on a global load of its bounds)
+    // kGroup consecutive slabs starting at kGroup*w, kGroup*(w + warps), ...
+    // Its groups, taken in order across the panel's tiles, are loaded one
+    // ahead: while a group is processed the next one (in this tile, or the
+    // warp's first of the next tile) is in flight.  tile starts: e0, e1 bound
+    // tile b, f1n the end of tile b + 1 (loaded a tile ahead of its use, so no
+    // tile waits on a global load of its bounds)
+    constexpr int kStep = kGroup * kConsumerWarps;
     int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
     int64_t f1n = a.B > 1 ? a.tstart[pb + 2] : e1;
     uint2 en[kGroup];
@@ -700,19 +703,24 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     for (int b = 0; ok && b < a.B; ++b) {
       const int nsl = (int)((e1 - e0) / kSlab);
-      uint2 e[kGroup];
-#pragma unroll
-      for (int j = 0; j < kGroup; ++j) e[j] = en[j];
       const int64_t f0 = e1;
       const int64_t f1 = b + 1 < a.B ? f1n : e1;
+      const int nsl_next = (int)((f1 - f0) / kSlab);
       if (b + 2 < a.B) f1n = a.tstart[pb + b + 3];
-      load_group(a.ent, f0, (int)((f1 - f0) / kSlab), kGroup * warp, lane, en);
+      // no group of this warp in tile b: its first of tile b + 1 goes in flight now
+      if (kGroup * warp >= nsl) load_group(a.ent, f0, nsl_next, kGroup * warp, lane, en);
       const int s = sb;
       if (!(ok = warp_wait(pot_full(s), ub, abort_w, a.err, 3))) break;
       if (++sb == kStages) { sb = 0; ub ^= 1u; }
       const float* cur = pot + (size_t)s * W;
-      for (int g = kGroup * warp; g < nsl; g += kGroup * kConsumerWarps) {
-        if (g != kGroup * warp) load_group(a.ent, e0, nsl, g, lane, e);
+      for (int g = kGroup * warp; g < nsl; g += kStep) {
+        uint2 e[kGroup];
+#pragma unroll
+        for (int j = 0; j < kGroup; ++j) e[j] = en[j];
+        if (g + kStep < nsl)
+          load_group(a.ent, e0, nsl, g + kStep, lane, en);
+        else
+          load_group(a.ent, f0, nsl_next, kGroup * warp, lane, en);
         process_group(smem, flags, cur, e, nsl - g, capd);
       }
       __syncwarp();
