@@ -88,7 +88,8 @@ int sinkslot_csr_workspace_bytes(int64_t nnz, int64_t nseg, int64_t* bytes_host)
  * `seg` is already non-decreasing (*was_sorted_host = 1).  Writes indptr
  * (nseg + 1, int32), idx = other[perm] as int16 (idx_bytes 2) or int32
  * (idx_bytes 4), vals[perm] (vals/out_vals nullable) and perm (int64,
- * nullable). */
+ * nullable).  With out_perm NULL (and vals given) the sort carries each
+ * entry's index and value instead of its position: no gather afterwards. */
 int sinkslot_coo_to_csr(const int64_t* seg, const int64_t* other, const float* vals, int64_t nnz,
                         int64_t nseg, int idx_bytes, void* workspace, int64_t workspace_bytes,
                         int32_t* indptr, void* idx, float* out_vals, int64_t* perm,

@@ -189,25 +189,25 @@ __device__ __forceinline__ uint32_t block_excl_scan256(uint32_t v, uint32_t* war
 // Dynamic shared memory of the scatter kernel: the tile's keys and values in
 // digit order (stable), then per-(warp, digit) counts, per-digit tile starts
 // and global run starts.
-template <typename K>
+template <typename K, typename V>
 constexpr size_t scatter_smem() {
-  return (size_t)kSortTile * (sizeof(K) + 4) + (size_t)kSortWarps * kRadix * 4 + kRadix * 4 +
-         kRadix * 8 + 64;
+  return (size_t)kSortTile * (sizeof(K) + sizeof(V)) + (size_t)kSortWarps * kRadix * 4 +
+         kRadix * 4 + kRadix * 8 + 64;
 }
 
 // One pass: the tile's keys are ranked (stable: warp match by digit, warps in
 // order), placed in shared memory in digit order, and written out run by run,
 // so consecutive threads store consecutive addresses of each digit's run.
-template <typename K>
+template <typename K, typename V>
 __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
-    const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, K* __restrict__ keys_out,
-    uint32_t* __restrict__ vals_out, int64_t seglen, int ntiles, int shift,
+    const K* __restrict__ keys_in, const V* __restrict__ vals_in, K* __restrict__ keys_out,
+    V* __restrict__ vals_out, int64_t seglen, int ntiles, int shift,
     const int64_t* __restrict__ offs) {
   extern __shared__ __align__(16) unsigned char sm[];
   K* skey = reinterpret_cast<K*>(sm);
-  uint32_t* sval = reinterpret_cast<uint32_t*>(sm + (size_t)kSortTile * sizeof(K));
+  V* sval = reinterpret_cast<V*>(sm + (size_t)kSortTile * sizeof(K));
   uint32_t(*wcnt)[kRadix] = reinterpret_cast<uint32_t(*)[kRadix]>(
-      sm + (size_t)kSortTile * (sizeof(K) + 4));
+      sm + (size_t)kSortTile * (sizeof(K) + sizeof(V)));
   uint32_t* dstart = reinterpret_cast<uint32_t*>(&wcnt[kSortWarps][0]);
   int64_t* gbase = reinterpret_cast<int64_t*>(dstart + kRadix);
   uint32_t* warp_tot = reinterpret_cast<uint32_t*>(gbase + kRadix);
@@ -221,14 +221,14 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
   const int64_t chunk = tile0 + (int64_t)warp * 32 * kSortItems;
   const uint32_t lt_mask = (1u << lane) - 1u;
   K key[kSortItems];
-  uint32_t val[kSortItems];
+  V val[kSortItems];
   uint32_t loc[kSortItems];
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
     const int64_t idx = chunk + r * 32 + lane;
     const bool valid = idx < seglen;
     key[r] = valid ? keys_in[segbase + idx] : K(0);
-    val[r] = valid ? (vals_in ? vals_in[segbase + idx] : (uint32_t)idx) : 0u;
+    val[r] = valid ? (vals_in ? vals_in[segbase + idx] : (V)idx) : V(0);
     const uint32_t dg = valid ? ((uint32_t)(key[r] >> shift) & 0xFFu) : 0x100u;
     const uint32_t peers = __match_any_sync(0xffffffffu, dg);
     const uint32_t rank = __popc(peers & lt_mask);
@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
   }
 }
 
-template <typename K>
-int radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, bool identity_vals,
+template <typename K, typename V>
+int radix_sort_pairs(K* keys, V* vals, K* keys_alt, V* vals_alt, bool identity_vals,
                      int64_t nseg, int64_t seglen, int key_bits, int64_t* hist, int64_t* scan_tmp,
                      bool* result_in_alt, cudaStream_t stream) {
   *result_in_alt = false;
@@ -294,16 +294,16 @@ int radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, b
     int dev = 0;
     SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-      SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(radix_scatter_kernel<K>,
+      SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(radix_scatter_kernel<K, V>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)scatter_smem<K>()));
+                                             (int)scatter_smem<K, V>()));
       if (dev >= 0 && dev < 64) configured[dev] = true;
     }
   }
   K* kin = keys;
-  uint32_t* vin = vals;
+  V* vin = vals;
   K* kout = keys_alt;
-  uint32_t* vout = vals_alt;
+  V* vout = vals_alt;
   bool first = true;
   bool in_alt = false;
   for (int shift = 0; shift < key_bits; shift += 8) {
@@ -311,21 +311,26 @@ int radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, b
     radix_hist_kernel<K><<<grid, kSortThreads, 0, stream>>>(kin, seglen, (int)ntiles, shift, hist);
     SINKSLOT_CHECK_LAUNCH();
     SINKSLOT_TRY(scan_exclusive_i64(hist, nh, scan_tmp, nullptr, stream));
-    radix_scatter_kernel<K><<<grid, kSortThreads, scatter_smem<K>(), stream>>>(
+    radix_scatter_kernel<K, V><<<grid, kSortThreads, scatter_smem<K, V>(), stream>>>(
         kin, (first && identity_vals) ? nullptr : vin, kout, vout, seglen, (int)ntiles, shift, hist);
     SINKSLOT_CHECK_LAUNCH();
     first = false;
     K* tk = kin; kin = kout; kout = tk;
-    uint32_t* tv = vin; vin = vout; vout = tv;
+    V* tv = vin; vin = vout; vout = tv;
     in_alt = !in_alt;
   }
   *result_in_alt = in_alt;
   return kOk;
 }
 
-template int radix_sort_pairs<uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*, bool, int64_t,
-                                        int64_t, int, int64_t*, int64_t*, bool*, cudaStream_t);
-template int radix_sort_pairs<uint64_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*, bool, int64_t,
-                                        int64_t, int, int64_t*, int64_t*, bool*, cudaStream_t);
+template int radix_sort_pairs<uint32_t, uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*, bool,
+                                                  int64_t, int64_t, int, int64_t*, int64_t*, bool*,
+                                                  cudaStream_t);
+template int radix_sort_pairs<uint64_t, uint32_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*, bool,
+                                                  int64_t, int64_t, int, int64_t*, int64_t*, bool*,
+                                                  cudaStream_t);
+template int radix_sort_pairs<uint32_t, uint64_t>(uint32_t*, uint64_t*, uint32_t*, uint64_t*, bool,
+                                                  int64_t, int64_t, int, int64_t*, int64_t*, bool*,
+                                                  cudaStream_t);
 
 }  // namespace sinkslot

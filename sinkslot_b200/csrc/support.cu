@@ -156,17 +156,42 @@ __global__ void chunk_parts_kernel(const uint32_t* __restrict__ order, const flo
   }
 }
 
-__global__ void chunk_carry_kernel(const float* __restrict__ parts, int C, int64_t nchunks,
-                                   int L, float* __restrict__ carry) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= C) return;
+// One block per row: the row's parts are staged in shared memory a window of
+// chunks at a time (coalesced), then thread 0 runs the carry chain -- the same
+// adds in the same order -- from registers, so no step of the serial chain
+// waits on a global load.
+constexpr int kCarryWin = 1024;  // chunks staged at a time
+constexpr int kMaxParts = 11;    // L + 1 parts per chunk, L = log_tx + 1 <= 10
+
+__global__ void __launch_bounds__(256) chunk_carry_kernel(const float* __restrict__ parts,
+                                                          int64_t nchunks, int L,
+                                                          float* __restrict__ carry) {
+  __shared__ float sp[kCarryWin * kMaxParts];
+  const int np = L + 1;
+  const int64_t row = blockIdx.x;
+  const float* P = parts + row * nchunks * np;
+  float* out = carry + row * nchunks;
   float c = 0.0f;
-  for (int64_t k = 0; k < nchunks; ++k) {
-    const float* P = parts + ((int64_t)row * nchunks + k) * (L + 1);
-    carry[(int64_t)row * nchunks + k] = c;
-    float T = __fadd_rn(P[0], c);
-    for (int j = 1; j <= L; ++j) T = __fadd_rn(P[j], T);
-    c = T;
+  for (int64_t k0 = 0; k0 < nchunks; k0 += kCarryWin) {
+    const int nk = (int)std::min<int64_t>(kCarryWin, nchunks - k0);
+    __syncthreads();  // the previous window is consumed
+    for (int i = threadIdx.x; i < nk * np; i += blockDim.x) sp[i] = P[k0 * np + i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll 4
+      for (int k = 0; k < nk; ++k) {
+        const float* q = sp + k * np;
+        float v[kMaxParts];
+#pragma unroll
+        for (int j = 0; j < kMaxParts; ++j) v[j] = j < np ? q[j] : 0.0f;
+        out[k0 + k] = c;
+        float T = __fadd_rn(v[0], c);
+#pragma unroll
+        for (int j = 1; j < kMaxParts; ++j)
+          if (j < np) T = __fadd_rn(v[j], T);
+        c = T;
+      }
+    }
   }
 }
 
@@ -231,8 +256,8 @@ static int slice_cumsum(const uint32_t* order, const float* w, float* out, int64
   chunk_parts_kernel<<<grid, tx, 2 * tx * sizeof(float), stream>>>(order, w, len, log_tx, nchunks,
                                                                     parts);
   SINKSLOT_CHECK_LAUNCH();
-  chunk_carry_kernel<<<(unsigned)ceil_div64(C, 64), 64, 0, stream>>>(parts, C, nchunks,
-                                                                      log_tx + 1, carry);
+  SINKSLOT_REQUIRE(log_tx + 2 <= kMaxParts, "cumsum: scan width out of range");
+  chunk_carry_kernel<<<(unsigned)C, 256, 0, stream>>>(parts, nchunks, log_tx + 1, carry);
   SINKSLOT_CHECK_LAUNCH();
   chunk_scan_kernel<<<grid, tx, 2 * tx * sizeof(float), stream>>>(order, w, out, len, log_tx,
                                                                    nchunks, carry);
@@ -680,6 +705,28 @@ __global__ void indptr_kernel(const T* __restrict__ skey, int64_t nnz, int64_t n
   }
 }
 
+// sort key (the segment) and the payload {other index, value bits} of each entry
+__global__ void key_payload_kernel(const int64_t* __restrict__ r, const int64_t* __restrict__ idx,
+                                   const float* __restrict__ vals, int64_t nnz,
+                                   uint32_t* __restrict__ k, uint64_t* __restrict__ pay) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    k[q] = (uint32_t)r[q];
+    pay[q] = (uint64_t)(uint32_t)idx[q] | ((uint64_t)__float_as_uint(vals[q]) << 32);
+  }
+}
+
+template <typename IT>
+__global__ void unpack_kernel(const uint64_t* __restrict__ pay, int64_t nnz, IT* __restrict__ oidx,
+                              float* __restrict__ ovals) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nnz;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t v = pay[q];
+    oidx[q] = (IT)(int32_t)(uint32_t)v;
+    ovals[q] = __uint_as_float((uint32_t)(v >> 32));
+  }
+}
+
 template <typename IT>
 __global__ void permute_kernel(const uint32_t* __restrict__ perm, const int64_t* __restrict__ idx,
                                const float* __restrict__ vals, int64_t nnz, IT* __restrict__ oidx,
@@ -695,7 +742,7 @@ __global__ void permute_kernel(const uint32_t* __restrict__ perm, const int64_t*
 
 size_t csr_workspace_bytes(int64_t nnz, int64_t nseg) {
   Carver cv(nullptr, 0);
-  cv.take<uint32_t>(nnz); cv.take<uint32_t>(nnz); cv.take<uint32_t>(nnz); cv.take<uint32_t>(nnz);
+  cv.take<uint32_t>(nnz); cv.take<uint64_t>(nnz); cv.take<uint32_t>(nnz); cv.take<uint64_t>(nnz);
   const int64_t nh = radix_hist_elems(1, std::max<int64_t>(nnz, 1));
   cv.take<int64_t>(nh);
   cv.take<int64_t>(scan_tmp_elems(nh));
@@ -711,10 +758,14 @@ int coo_to_csr(const int64_t* seg, const int64_t* idx, const float* vals, int64_
   SINKSLOT_REQUIRE(nseg >= 0 && nseg < (int64_t(1) << 31) && nnz >= 0 && nnz < (int64_t(1) << 31),
                    "to_csr: sizes must be < 2^31");
   Carver cv(ws, ws_bytes);
+  // values of the sort: the entry's position (uint32) when the permutation is
+  // asked for, else the payload {other index, value bits} (uint64)
   uint32_t* k1 = cv.take<uint32_t>(nnz);
-  uint32_t* v1 = cv.take<uint32_t>(nnz);
+  uint64_t* p1 = cv.take<uint64_t>(nnz);
   uint32_t* k2 = cv.take<uint32_t>(nnz);
-  uint32_t* v2 = cv.take<uint32_t>(nnz);
+  uint64_t* p2 = cv.take<uint64_t>(nnz);
+  uint32_t* v1 = reinterpret_cast<uint32_t*>(p1);
+  uint32_t* v2 = reinterpret_cast<uint32_t*>(p2);
   const int64_t nh = radix_hist_elems(1, std::max<int64_t>(nnz, 1));
   int64_t* hist = cv.take<int64_t>(nh);
   int64_t* stmp = cv.take<int64_t>(scan_tmp_elems(nh));
@@ -732,6 +783,28 @@ int coo_to_csr(const int64_t* seg, const int64_t* idx, const float* vals, int64_
     SINKSLOT_CUDA_TRY(cudaStreamSynchronize(stream));
   }
   *was_sorted = unsorted ? 0 : 1;
+  if (unsorted && !out_perm && vals && out_vals) {
+    // no permutation wanted: the sort carries each entry's index and value, so
+    // nothing is gathered from random positions afterwards
+    key_payload_kernel<<<grid_for(nnz, 256), 256, 0, stream>>>(seg, idx, vals, nnz, k1, p1);
+    SINKSLOT_CHECK_LAUNCH();
+    bool alt = false;
+    SINKSLOT_TRY((radix_sort_pairs<uint32_t, uint64_t>(
+        k1, p1, k2, p2, false, 1, nnz, bits_for((uint64_t)std::max<int64_t>(nseg, 1)), hist,
+        stmp, &alt, stream)));
+    const uint32_t* sk = alt ? k2 : k1;
+    const uint64_t* sp = alt ? p2 : p1;
+    indptr_kernel<uint32_t><<<grid_for(nseg + 1, 256), 256, 0, stream>>>(sk, nnz, nseg, out_ptr);
+    SINKSLOT_CHECK_LAUNCH();
+    if (idx_bytes == 2)
+      unpack_kernel<int16_t><<<grid_for(nnz, 256), 256, 0, stream>>>(
+          sp, nnz, static_cast<int16_t*>(out_idx), out_vals);
+    else
+      unpack_kernel<int32_t><<<grid_for(nnz, 256), 256, 0, stream>>>(
+          sp, nnz, static_cast<int32_t*>(out_idx), out_vals);
+    SINKSLOT_CHECK_LAUNCH();
+    return kOk;
+  }
   const uint32_t* perm = nullptr;
   if (!unsorted) {
     indptr_kernel<int64_t><<<grid_for(nseg + 1, 256), 256, 0, stream>>>(seg, nnz, nseg, out_ptr);

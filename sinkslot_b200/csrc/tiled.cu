@@ -119,6 +119,15 @@ static size_t pipe_smem(int R, int W) {
   return rows_smem(R) + (size_t)kStages * (size_t)W * 4 + kBarBytes;
 }
 
+// The direct builder (one CTA per panel) keeps in shared memory a counter per
+// (bank, block), the panel's CSR offsets and its tile starts.
+constexpr int kBanks = 32;
+constexpr int kBuildThreads = 32 * kBanks;  // warp w walks the rows of bank w
+constexpr size_t kDirectSmemCap = 200 * 1024;
+static size_t direct_smem(int R, int B) {
+  return (size_t)kBanks * B * 4 + align_up((size_t)(R + 2) * 4, 16) + (size_t)(B + 1) * 8 + 64;
+}
+
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   TileGeom g;
   g.nseg = nseg;
@@ -152,14 +161,20 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
   cv.take<uint2>(std::max<int64_t>(g.cap, 1));  // entries {meta, lam bits}
   g.layout_bytes = cv.used;
+  g.direct = direct_smem(g.R, g.B) <= kDirectSmemCap;
   Carver bw(nullptr, 0);
-  const int64_t e = std::max<int64_t>(nnz, 1);
-  bw.take<uint32_t>(e);  // row id
-  for (int i = 0; i < 4; ++i) bw.take<uint32_t>(e);  // keys / values of the sort
-  const int64_t nh = radix_hist_elems(1, e);
-  bw.take<int64_t>(std::max<int64_t>(nh, ntiles + 2));
-  bw.take<int64_t>(scan_tmp_elems(std::max<int64_t>(nh, ntiles + 2)));
-  bw.take<int64_t>(ntiles + 2);  // unpadded tile starts
+  if (g.direct) {
+    bw.take<uint32_t>(ntiles * kBanks);            // per panel, bank and block: entries
+    bw.take<int64_t>(scan_tmp_elems(ntiles + 1));  // scan of the tile sizes
+  } else {
+    const int64_t e = std::max<int64_t>(nnz, 1);
+    bw.take<uint32_t>(e);  // row id
+    for (int i = 0; i < 4; ++i) bw.take<uint32_t>(e);  // keys / values of the sort
+    const int64_t nh = radix_hist_elems(1, e);
+    bw.take<int64_t>(std::max<int64_t>(nh, ntiles + 2));
+    bw.take<int64_t>(scan_tmp_elems(std::max<int64_t>(nh, ntiles + 2)));
+    bw.take<int64_t>(ntiles + 2);  // unpadded tile starts
+  }
   g.build_bytes = bw.used;
   return g;
 }
@@ -290,6 +305,193 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
   }
 }
 
+// ---------------------------------------------------------------------------
+// direct builder: one CTA per panel, no sort
+// ---------------------------------------------------------------------------
+// Warp w walks the panel's rows of bank w (rows w, w + 32, ...) in order and
+// each row's entries in order, so the entries of a (block, bank) bucket are
+// met in CSR order -- the order of the stable sort above -- and the layout is
+// the same entry for entry.  Shared memory: cnt[kBanks][B] (uint32), the
+// panel's CSR offsets ps[0..rows] (int32), its tile starts ts[0..B] (int64).
+struct PanelSmem {
+  uint32_t* cnt;
+  int32_t* ps;
+  int64_t* ts;
+};
+
+__device__ __forceinline__ PanelSmem panel_smem(unsigned char* sm, int R, int B) {
+  PanelSmem d;
+  d.cnt = reinterpret_cast<uint32_t*>(sm);
+  d.ps = reinterpret_cast<int32_t*>(sm + (size_t)kBanks * B * 4);
+  d.ts = reinterpret_cast<int64_t*>(sm + (size_t)kBanks * B * 4 +
+                                    align_up((size_t)(R + 2) * 4, 16));
+  return d;
+}
+
+// Per panel: entries per (bank, block) into cnt_out[p][bank][block], padded
+// tile sizes into tsize[p * B + b], and the longest row of at most
+// kMaxTiledRow entries into *longest.
+template <typename IT>
+__global__ void __launch_bounds__(kBuildThreads) panel_count_kernel(
+    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, int64_t nseg, int R, int B,
+    int logW, uint32_t* __restrict__ cnt_out, int64_t* __restrict__ tsize,
+    unsigned long long* __restrict__ longest) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  const PanelSmem d = panel_smem(sm, R, B);
+  const int p = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row0 = (int64_t)p * R;
+  const int rows = (int)std::max<int64_t>(0, std::min<int64_t>(R, nseg - row0));
+  for (int i = tid; i < kBanks * B; i += kBuildThreads) d.cnt[i] = 0;
+  for (int i = tid; i <= rows; i += kBuildThreads) d.ps[i] = ptr[row0 + i];
+  __syncthreads();
+  unsigned long long best = 0;
+  for (int r = tid; r < rows; r += kBuildThreads) {
+    const unsigned long long len = (unsigned long long)(d.ps[r + 1] - d.ps[r]);
+    if (len <= (unsigned long long)kMaxTiledRow && len > best) best = len;
+  }
+  for (int o = 16; o >= 1; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+    best = t > best ? t : best;
+  }
+  if (lane == 0 && best > 0) atomicMax(longest, best);
+  uint32_t* cw = d.cnt + warp * B;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int r = warp; r < rows; r += kBanks) {
+    const int s = d.ps[r], e = d.ps[r + 1];
+    for (int k0 = s; k0 < e; k0 += 32) {
+      const int k = k0 + lane;
+      uint32_t b = k < e ? ((uint32_t)(int32_t)idx[k] >> logW) : 0xFFFFFFFFu;
+      const bool v = b < (uint32_t)B;  // an index outside [0, m_other) is left out
+      if (!v) b = 0xFFFFFFFFu;
+      const uint32_t peers = __match_any_sync(0xffffffffu, b);
+      if (v && (peers & lt) == 0) cw[b] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  uint32_t* co = cnt_out + (int64_t)p * kBanks * B;
+  for (int i = tid; i < kBanks * B; i += kBuildThreads) co[i] = d.cnt[i];
+  for (int b = tid; b < B; b += kBuildThreads) {
+    uint32_t t = 0;
+    for (int w = 0; w < kBanks; ++w) t += d.cnt[w * B + b];
+    tsize[(int64_t)p * B + b] = (int64_t)((t + kSlab - 1) & ~(uint32_t)(kSlab - 1));
+  }
+}
+
+// Per panel: every entry to its slot (sorted position q of its tile goes to
+// slab q mod N, lane q / N), and the tile's padding to the slots after them.
+template <typename IT>
+__global__ void __launch_bounds__(kBuildThreads) panel_scatter_kernel(
+    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, const float* __restrict__ lam,
+    int64_t nseg, int R, int B, int logW, const uint32_t* __restrict__ cnt_in,
+    const int64_t* __restrict__ tstart, uint2* __restrict__ ent) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  const PanelSmem d = panel_smem(sm, R, B);
+  const int p = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row0 = (int64_t)p * R;
+  const int rows = (int)std::max<int64_t>(0, std::min<int64_t>(R, nseg - row0));
+  for (int i = tid; i <= rows; i += kBuildThreads) d.ps[i] = ptr[row0 + i];
+  for (int b = tid; b <= B; b += kBuildThreads) d.ts[b] = tstart[(int64_t)p * B + b];
+  __syncthreads();
+  const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
+  const uint32_t* ci = cnt_in + (int64_t)p * kBanks * B;
+  for (int b = tid; b < B; b += kBuildThreads) {
+    // each bank's first sorted position in the tile; padding after the entries
+    uint32_t run = 0;
+    for (int w = 0; w < kBanks; ++w) {
+      const uint32_t c = ci[w * B + b];
+      d.cnt[w * B + b] = run;
+      run += c;
+    }
+    const int64_t t0 = d.ts[b];
+    const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
+    for (uint32_t q = run; q < ns * kSlab; ++q) {
+      const uint32_t ln = q / ns;
+      ent[t0 + ((int64_t)(q - ln * ns) << 5) + ln] = pad;
+    }
+  }
+  __syncthreads();
+  const uint32_t wmask = (1u << logW) - 1u;
+  uint32_t* cw = d.cnt + warp * B;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int r = warp; r < rows; r += kBanks) {
+    const int s = d.ps[r], e = d.ps[r + 1];
+    for (int k0 = s; k0 < e; k0 += 32) {
+      const int k = k0 + lane;
+      const uint32_t c = k < e ? (uint32_t)(int32_t)idx[k] : 0xFFFFFFFFu;
+      uint32_t b = c >> logW;
+      const bool v = k < e && b < (uint32_t)B;  // as in panel_count_kernel
+      if (!v) b = 0xFFFFFFFFu;
+      const float lv = v ? lam[k] : 0.0f;
+      const uint32_t peers = __match_any_sync(0xffffffffu, b);
+      const uint32_t base = v ? cw[b] : 0u;
+      __syncwarp();
+      if (v && (peers & lt) == 0) cw[b] = base + __popc(peers);
+      __syncwarp();
+      if (v) {
+        const uint32_t q = base + __popc(peers & lt);
+        const int64_t t0 = d.ts[b];
+        const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
+        const uint32_t ln = q / ns;
+        ent[t0 + ((int64_t)(q - ln * ns) << 5) + ln] =
+            make_uint2(((uint32_t)r << 16) | (c & wmask), __float_as_uint(lv));
+      }
+    }
+  }
+}
+
+// padding entries after the last tile: [*end, cap)
+__global__ void fill_tail_kernel(uint2* __restrict__ ent, const int64_t* __restrict__ end,
+                                 int64_t cap, int R) {
+  const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
+  for (int64_t q = *end + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < cap;
+       q += (int64_t)gridDim.x * blockDim.x)
+    ent[q] = pad;
+}
+
+template <typename IT>
+static int build_tiles_direct(const int32_t* ptr, const IT* idx, const float* lam,
+                              const TileGeom& g, const LayoutPtrs& L, void* ws, size_t ws_bytes,
+                              cudaStream_t st) {
+  const int64_t ntiles = (int64_t)g.P * g.B;
+  Carver cv(ws, ws_bytes);
+  uint32_t* cnt = cv.take<uint32_t>(ntiles * kBanks);
+  int64_t* stmp = cv.take<int64_t>(scan_tmp_elems(ntiles + 1));
+  if (!cv.ok) {
+    set_error("build_tiles: workspace too small");
+    return kWorkspaceTooSmall;
+  }
+  const size_t smem = direct_smem(g.R, g.B);
+  {
+    // the dynamic shared-memory limit is a per-device function attribute
+    static bool configured[64] = {};
+    int dev = 0;
+    SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+      SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(panel_count_kernel<IT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kDirectSmemCap));
+      SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(panel_scatter_kernel<IT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kDirectSmemCap));
+      if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+  }
+  SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.header, 0, 8 * sizeof(int64_t), st));
+  panel_count_kernel<IT><<<(unsigned)g.P, kBuildThreads, smem, st>>>(
+      ptr, idx, g.nseg, g.R, g.B, g.logW, cnt, L.tstart,
+      reinterpret_cast<unsigned long long*>(L.header));
+  SINKSLOT_CHECK_LAUNCH();
+  SINKSLOT_TRY(scan_exclusive_i64(L.tstart, ntiles, stmp, L.tstart + ntiles, st));
+  panel_scatter_kernel<IT><<<(unsigned)g.P, kBuildThreads, smem, st>>>(
+      ptr, idx, lam, g.nseg, g.R, g.B, g.logW, cnt, L.tstart, L.ent);
+  SINKSLOT_CHECK_LAUNCH();
+  fill_tail_kernel<<<grid_t(ntiles * (kSlab - 1) + 1, 256), 256, 0, st>>>(L.ent, L.tstart + ntiles,
+                                                                          g.cap, g.R);
+  SINKSLOT_CHECK_LAUNCH();
+  return kOk;
+}
+
 int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float* lam,
                 const TileGeom& g, void* layout, void* ws, size_t ws_bytes, cudaStream_t st) {
   SINKSLOT_REQUIRE(idx_bytes == 2 || idx_bytes == 4, "build_tiles: idx_bytes must be 2 or 4");
@@ -298,6 +500,11 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
   SINKSLOT_REQUIRE((int64_t)g.P * g.B < (int64_t(1) << (32 - kBankBits)),
                    "build_tiles: too many tiles");
   LayoutPtrs L = carve_layout(layout, g);
+  if (g.direct) {
+    if (idx_bytes == 2)
+      return build_tiles_direct(ptr, static_cast<const int16_t*>(idx), lam, g, L, ws, ws_bytes, st);
+    return build_tiles_direct(ptr, static_cast<const int32_t*>(idx), lam, g, L, ws, ws_bytes, st);
+  }
   Carver cv(ws, ws_bytes);
   const int64_t e = std::max<int64_t>(g.nnz, 1);
   const int64_t ntiles = (int64_t)g.P * g.B;

@@ -32,7 +32,7 @@ from . import _lib
 from ._lib import call, ptr, stream_of
 from .sinkhorn_solvers import (SinkslotSolveResult, _idx_bytes, _resolve_stop_mode, _validate,
                                build_tiles, tiles_pay_off)
-from .solver import cost_and_lam, sot_plan_coo, to_csr
+from .solver import _to_csr, cost_and_lam, sot_plan_coo
 
 MAX_RANKS = 8
 _CHECK_CODE = {"fixed": 0, "potential": 1, "marginal": 2}
@@ -208,8 +208,8 @@ class ShardedSolver:
             raise ValueError(f"ranks built different supports {sizes}: inputs must be identical")
         lam, _ = cost_and_lam(X, Y, self.rows, self.cols, self.S, eps)
         self.log_a, self.log_b = a.log().contiguous(), b.log().contiguous()
-        r_ptr, r_idx, r_lam, _ = to_csr(self.rows, self.cols, lam, n, narrow_key=True)
-        c_ptr, c_idx, c_lam, _ = to_csr(self.cols, self.rows, lam, m, narrow_key=True)
+        r_ptr, r_idx, r_lam, _ = _to_csr(self.rows, self.cols, lam, n, want_perm=False)
+        c_ptr, c_idx, c_lam, _ = _to_csr(self.cols, self.rows, lam, m, want_perm=False)
         self.r0, self.nr = shard_bounds(n, self.world, self.rank)
         self.c0, self.nc = shard_bounds(m, self.world, self.rank)
         self.row = slice_csr(r_ptr, r_idx, r_lam, self.r0, self.nr)

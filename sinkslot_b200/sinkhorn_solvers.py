@@ -21,7 +21,7 @@ from jaxtyping import Float, jaxtyped
 
 from . import _lib
 from ._lib import call, ptr, stream_of
-from .solver import cost_and_lam, sot_plan_coo, to_csr
+from .solver import _to_csr, cost_and_lam, sot_plan_coo, to_csr
 
 BACKENDS = ("auto", "b200", "triton")
 
@@ -258,8 +258,8 @@ def sinkslot_solve(X: Float[torch.Tensor, "n d"], Y: Float[torch.Tensor, "m d"],
     rows, cols, S = sot_plan_coo(X, Y, a, b, L=L, seed=seed, chunk=chunk)
     lam, _ = cost_and_lam(X, Y, rows, cols, S, eps)
     log_a, log_b = a.log(), b.log()
-    r_ptr, r_idx, r_lam, _ = to_csr(rows, cols, lam, n, narrow_key=True)
-    c_ptr, c_idx, c_lam, _ = to_csr(cols, rows, lam, m, narrow_key=True)
+    r_ptr, r_idx, r_lam, _ = _to_csr(rows, cols, lam, n, want_perm=False)
+    c_ptr, c_idx, c_lam, _ = _to_csr(cols, rows, lam, m, want_perm=False)
     nnz = rows.numel()
     tiles = (build_tiles(r_ptr, r_idx, r_lam, n, m) if tiles_pay_off(n, m, nnz) else None,
              build_tiles(c_ptr, c_idx, c_lam, m, n) if tiles_pay_off(m, n, nnz) else None)

@@ -188,6 +188,13 @@ def to_csr(rows: torch.Tensor, cols: torch.Tensor, vals: torch.Tensor, n: int,
     int16 when its maximum is below 2**15, else int32.  ``narrow_key`` is
     accepted for compatibility (the sort key is always 32-bit here).
     """
+    return _to_csr(rows, cols, vals, n, want_perm=True)
+
+
+def _to_csr(rows: torch.Tensor, cols: torch.Tensor, vals: torch.Tensor, n: int,
+            want_perm: bool):
+    """``to_csr``; without ``want_perm`` the permutation is not formed (None)
+    and the sort carries the indices and values themselves."""
     if not rows.is_cuda:
         raise ValueError("to_csr: sinkslot_b200 runs on CUDA tensors only")
     dev = rows.device
@@ -205,12 +212,13 @@ def to_csr(rows: torch.Tensor, cols: torch.Tensor, vals: torch.Tensor, n: int,
     indptr = torch.empty(n + 1, dtype=torch.int32, device=dev)
     idx = torch.empty(nnz, dtype=idx_dtype, device=dev)
     out_vals = torch.empty_like(vals)
-    perm = torch.empty(nnz, dtype=torch.int64, device=dev)
+    perm = torch.empty(nnz, dtype=torch.int64, device=dev) if want_perm else None
     was_sorted = ctypes.c_int(0)
     with torch.cuda.device(dev):
         call("sinkslot_coo_to_csr", ptr(rows), ptr(cols), ptr(vals), nnz, n,
              2 if idx_dtype == torch.int16 else 4, ptr(ws), ws.numel(), ptr(indptr), ptr(idx),
-             ptr(out_vals), ptr(perm), ctypes.byref(was_sorted), stream_of(dev))
+             ptr(out_vals), ptr(perm) if want_perm else None, ctypes.byref(was_sorted),
+             stream_of(dev))
     if was_sorted.value:
         return indptr, idx, vals, None
     return indptr, idx, out_vals, perm

@@ -180,3 +180,26 @@ def test_to_csr_matches_oracle(cuda, oracle, sorted_rows, nseg, nnz, maxidx):
     assert (perm is None) == (operm is None)
     if perm is not None:
         np.testing.assert_array_equal(perm.cpu().numpy(), operm)
+
+
+@pytest.mark.parametrize("sorted_rows", [True, False])
+@pytest.mark.parametrize("nseg,nnz,maxidx", [(1000, 20000, 30000), (70000, 500000, 1 << 20),
+                                             (5, 0, 10), (3, 1, 7)])
+def test_csr_without_permutation_matches_oracle(cuda, oracle, sorted_rows, nseg, nnz, maxidx):
+    """The solve's CSR/CSC path (no permutation formed; the sort carries index
+    and value) gives the same arrays as to_csr."""
+    from sinkslot_b200.solver import _to_csr
+    g = torch.Generator().manual_seed(7 * nseg + nnz)
+    rows = torch.randint(0, nseg, (nnz,), generator=g)
+    if sorted_rows:
+        rows, _ = torch.sort(rows)
+    cols = torch.randint(0, maxidx, (nnz,), generator=g)
+    vals = torch.randn(nnz, generator=g)
+    vals[::97] = -float("inf")
+    ptr, idx, v, perm = _to_csr(rows.to(cuda), cols.to(cuda), vals.to(cuda), nseg, want_perm=False)
+    assert perm is None
+    optr, oidx, ov, _ = oracle.to_csr(rows.numpy(), cols.numpy(), vals.numpy(), nseg)
+    np.testing.assert_array_equal(ptr.cpu().numpy(), optr)
+    assert idx.dtype == {np.int16: torch.int16, np.int32: torch.int32}[oidx.dtype.type]
+    np.testing.assert_array_equal(idx.cpu().numpy(), oidx)
+    np.testing.assert_array_equal(v.cpu().numpy().view(np.uint32), ov.view(np.uint32))
