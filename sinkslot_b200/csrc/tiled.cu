@@ -119,13 +119,16 @@ static size_t pipe_smem(int R, int W) {
   return rows_smem(R) + (size_t)kStages * (size_t)W * 4 + kBarBytes;
 }
 
-// The direct builder (one CTA per panel) keeps in shared memory a counter per
-// (bank, block), the panel's CSR offsets and its tile starts.
+// The direct builder cuts each panel into S sub-panels of Rs consecutive rows,
+// one CTA each, which keeps in shared memory two counters per (bank, block),
+// the sub-panel's CSR offsets and the panel's tile starts.
 constexpr int kBanks = 32;
 constexpr int kBuildThreads = 32 * kBanks;  // warp w walks the rows of bank w
-constexpr size_t kDirectSmemCap = 200 * 1024;
-static size_t direct_smem(int R, int B) {
-  return (size_t)kBanks * B * 4 + align_up((size_t)(R + 2) * 4, 16) + (size_t)(B + 1) * 8 + 64;
+constexpr int kBuildCtasPerSm = 8;          // sub-panels enough for this many CTAs per SM
+constexpr size_t kDirectSmemCap = 96 * 1024;
+static size_t direct_smem(int Rs, int B) {
+  return 2 * (size_t)kBanks * B * 4 + align_up((size_t)(Rs + 2) * 4, 16) + (size_t)(B + 1) * 8 +
+         64;
 }
 
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
@@ -161,10 +164,13 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
   cv.take<uint2>(std::max<int64_t>(g.cap, 1));  // entries {meta, lam bits}
   g.layout_bytes = cv.used;
-  g.direct = direct_smem(g.R, g.B) <= kDirectSmemCap;
+  g.S = (int)std::min<int64_t>(16, std::max<int64_t>(1, ceil_div64((int64_t)kBuildCtasPerSm * sms,
+                                                                     g.P)));
+  g.S = (int)std::min<int64_t>(g.S, std::max<int64_t>(1, g.R / 64));  // >= 2 rows per warp
+  g.direct = direct_smem((int)ceil_div64(g.R, g.S), g.B) <= kDirectSmemCap;
   Carver bw(nullptr, 0);
   if (g.direct) {
-    bw.take<uint32_t>(ntiles * kBanks);            // per panel, bank and block: entries
+    bw.take<uint32_t>(ntiles * g.S * kBanks);      // per sub-panel, bank and block: entries
     bw.take<int64_t>(scan_tmp_elems(ntiles + 1));  // scan of the tile sizes
   } else {
     const int64_t e = std::max<int64_t>(nnz, 1);
@@ -306,47 +312,65 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
 }
 
 // ---------------------------------------------------------------------------
-// direct builder: one CTA per panel, no sort
+// direct builder: one CTA per sub-panel, no sort
 // ---------------------------------------------------------------------------
-// Warp w walks the panel's rows of bank w (rows w, w + 32, ...) in order and
-// each row's entries in order, so the entries of a (block, bank) bucket are
-// met in CSR order -- the order of the stable sort above -- and the layout is
-// the same entry for entry.  Shared memory: cnt[kBanks][B] (uint32), the
-// panel's CSR offsets ps[0..rows] (int32), its tile starts ts[0..B] (int64).
+// Warp w walks the sub-panel's rows of bank w (panel rows r = w mod 32) in
+// order and each row's entries in order; sub-panels follow one another in row
+// order.  So the entries of a (block, bank) bucket are met in CSR order -- the
+// order of the stable sort above -- and the layout is the same entry for
+// entry.  Shared memory: two uint32 counters per (bank, block) -- the running
+// slot and a scratch --, the sub-panel's CSR offsets ps[0..nr] (int32), the
+// panel's tile starts ts[0..B] (int64).
 struct PanelSmem {
   uint32_t* cnt;
+  uint32_t* tmp;
   int32_t* ps;
   int64_t* ts;
 };
 
-__device__ __forceinline__ PanelSmem panel_smem(unsigned char* sm, int R, int B) {
+__device__ __forceinline__ PanelSmem panel_smem(unsigned char* sm, int Rs, int B) {
   PanelSmem d;
   d.cnt = reinterpret_cast<uint32_t*>(sm);
-  d.ps = reinterpret_cast<int32_t*>(sm + (size_t)kBanks * B * 4);
-  d.ts = reinterpret_cast<int64_t*>(sm + (size_t)kBanks * B * 4 +
-                                    align_up((size_t)(R + 2) * 4, 16));
+  d.tmp = d.cnt + kBanks * B;
+  d.ps = reinterpret_cast<int32_t*>(sm + 2 * (size_t)kBanks * B * 4);
+  d.ts = reinterpret_cast<int64_t*>(sm + 2 * (size_t)kBanks * B * 4 +
+                                    align_up((size_t)(Rs + 2) * 4, 16));
   return d;
 }
 
-// Per panel: entries per (bank, block) into cnt_out[p][bank][block], padded
-// tile sizes into tsize[p * B + b], and the longest row of at most
-// kMaxTiledRow entries into *longest.
+// The rows of sub-panel s of panel p: panel-local [r_lo, r_hi).
+struct SubRows {
+  int64_t row0;  // first row of the panel
+  int r_lo, r_hi;
+};
+
+__device__ __forceinline__ SubRows sub_rows(int64_t nseg, int R, int Rs) {
+  SubRows q;
+  q.row0 = (int64_t)blockIdx.y * R;
+  const int rows = (int)std::max<int64_t>(0, std::min<int64_t>(R, nseg - q.row0));
+  q.r_lo = std::min((int)blockIdx.x * Rs, rows);
+  q.r_hi = std::min(q.r_lo + Rs, rows);
+  return q;
+}
+
+// Per sub-panel (blockIdx.x of gridDim.x, panel blockIdx.y): entries per
+// (bank, block) into cnt_out[(p * S + s) * kBanks + bank][block], and the
+// longest row of at most kMaxTiledRow entries into *longest.
 template <typename IT>
-__global__ void __launch_bounds__(kBuildThreads) panel_count_kernel(
-    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, int64_t nseg, int R, int B,
-    int logW, uint32_t* __restrict__ cnt_out, int64_t* __restrict__ tsize,
-    unsigned long long* __restrict__ longest) {
+__global__ void __launch_bounds__(kBuildThreads, 2) panel_count_kernel(
+    const int32_t* __restrict__ ptr, const IT* __restrict__ idx, int64_t nseg, int R, int Rs,
+    int B, int logW, uint32_t* __restrict__ cnt_out, unsigned long long* __restrict__ longest) {
   extern __shared__ __align__(16) unsigned char sm[];
-  const PanelSmem d = panel_smem(sm, R, B);
-  const int p = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t row0 = (int64_t)p * R;
-  const int rows = (int)std::max<int64_t>(0, std::min<int64_t>(R, nseg - row0));
+  const PanelSmem d = panel_smem(sm, Rs, B);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const SubRows q = sub_rows(nseg, R, Rs);
+  const int nr = q.r_hi - q.r_lo;
   for (int i = tid; i < kBanks * B; i += kBuildThreads) d.cnt[i] = 0;
-  for (int i = tid; i <= rows; i += kBuildThreads) d.ps[i] = ptr[row0 + i];
+  for (int i = tid; i <= nr; i += kBuildThreads) d.ps[i] = ptr[q.row0 + q.r_lo + i];
   __syncthreads();
   unsigned long long best = 0;
-  for (int r = tid; r < rows; r += kBuildThreads) {
-    const unsigned long long len = (unsigned long long)(d.ps[r + 1] - d.ps[r]);
+  for (int i = tid; i < nr; i += kBuildThreads) {
+    const unsigned long long len = (unsigned long long)(d.ps[i + 1] - d.ps[i]);
     if (len <= (unsigned long long)kMaxTiledRow && len > best) best = len;
   }
   for (int o = 16; o >= 1; o >>= 1) {
@@ -356,8 +380,8 @@ __global__ void __launch_bounds__(kBuildThreads) panel_count_kernel(
   if (lane == 0 && best > 0) atomicMax(longest, best);
   uint32_t* cw = d.cnt + warp * B;
   const uint32_t lt = (1u << lane) - 1u;
-  for (int r = warp; r < rows; r += kBanks) {
-    const int s = d.ps[r], e = d.ps[r + 1];
+  for (int r = q.r_lo + ((warp - q.r_lo) & (kBanks - 1)); r < q.r_hi; r += kBanks) {
+    const int s = d.ps[r - q.r_lo], e = d.ps[r - q.r_lo + 1];
     for (int k0 = s; k0 < e; k0 += 32) {
       const int k = k0 + lane;
       uint32_t b = k < e ? ((uint32_t)(int32_t)idx[k] >> logW) : 0xFFFFFFFFu;
@@ -369,54 +393,79 @@ __global__ void __launch_bounds__(kBuildThreads) panel_count_kernel(
     }
   }
   __syncthreads();
-  uint32_t* co = cnt_out + (int64_t)p * kBanks * B;
+  uint32_t* co = cnt_out + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * kBanks * B;
   for (int i = tid; i < kBanks * B; i += kBuildThreads) co[i] = d.cnt[i];
-  for (int b = tid; b < B; b += kBuildThreads) {
-    uint32_t t = 0;
-    for (int w = 0; w < kBanks; ++w) t += d.cnt[w * B + b];
-    tsize[(int64_t)p * B + b] = (int64_t)((t + kSlab - 1) & ~(uint32_t)(kSlab - 1));
+}
+
+// tsize[t] = entries of tile t = p * B + b over its panel's S sub-panels and
+// the banks, rounded up to a slab
+__global__ void tile_size_kernel(const uint32_t* __restrict__ cnt, int64_t ntiles, int B, int S,
+                                 int64_t* __restrict__ tsize) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ntiles;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = t / B, b = t - p * B;
+    const uint32_t* c = cnt + p * S * kBanks * B + b;
+    uint32_t n = 0;
+    for (int i = 0; i < S * kBanks; ++i) n += c[(int64_t)i * B];
+    tsize[t] = (int64_t)((n + kSlab - 1) & ~(uint32_t)(kSlab - 1));
   }
 }
 
-// Per panel: every entry to its slot (sorted position q of its tile goes to
-// slab q mod N, lane q / N), and the tile's padding to the slots after them.
+// Per sub-panel: every entry to its slot (sorted position q of its tile goes to
+// slab q mod N, lane q / N); sub-panel 0 also writes the tile's padding to the
+// slots after its entries.
 template <typename IT>
-__global__ void __launch_bounds__(kBuildThreads) panel_scatter_kernel(
+__global__ void __launch_bounds__(kBuildThreads, 1) panel_scatter_kernel(
     const int32_t* __restrict__ ptr, const IT* __restrict__ idx, const float* __restrict__ lam,
-    int64_t nseg, int R, int B, int logW, const uint32_t* __restrict__ cnt_in,
+    int64_t nseg, int R, int Rs, int B, int logW, const uint32_t* __restrict__ cnt_in,
     const int64_t* __restrict__ tstart, uint2* __restrict__ ent) {
   extern __shared__ __align__(16) unsigned char sm[];
-  const PanelSmem d = panel_smem(sm, R, B);
-  const int p = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t row0 = (int64_t)p * R;
-  const int rows = (int)std::max<int64_t>(0, std::min<int64_t>(R, nseg - row0));
-  for (int i = tid; i <= rows; i += kBuildThreads) d.ps[i] = ptr[row0 + i];
-  for (int b = tid; b <= B; b += kBuildThreads) d.ts[b] = tstart[(int64_t)p * B + b];
+  const PanelSmem d = panel_smem(sm, Rs, B);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = gridDim.x, s = blockIdx.x;
+  const int64_t p = blockIdx.y;
+  const SubRows q = sub_rows(nseg, R, Rs);
+  const int nr = q.r_hi - q.r_lo;
+  for (int i = tid; i <= nr; i += kBuildThreads) d.ps[i] = ptr[q.row0 + q.r_lo + i];
+  for (int b = tid; b <= B; b += kBuildThreads) d.ts[b] = tstart[p * B + b];
+  // per (bank, block): the entries of the earlier sub-panels (cnt) and of all
+  // sub-panels (tmp)
+  const uint32_t* ci = cnt_in + p * S * kBanks * B;
+  for (int i = tid; i < kBanks * B; i += kBuildThreads) {
+    uint32_t pre = 0, all = 0;
+    for (int u = 0; u < S; ++u) {
+      const uint32_t c = ci[(int64_t)u * kBanks * B + i];
+      pre += u < s ? c : 0u;
+      all += c;
+    }
+    d.cnt[i] = pre;
+    d.tmp[i] = all;
+  }
   __syncthreads();
   const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
-  const uint32_t* ci = cnt_in + (int64_t)p * kBanks * B;
   for (int b = tid; b < B; b += kBuildThreads) {
     // each bank's first sorted position in the tile; padding after the entries
     uint32_t run = 0;
     for (int w = 0; w < kBanks; ++w) {
-      const uint32_t c = ci[w * B + b];
-      d.cnt[w * B + b] = run;
-      run += c;
+      d.cnt[w * B + b] += run;
+      run += d.tmp[w * B + b];
     }
-    const int64_t t0 = d.ts[b];
-    const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
-    for (uint32_t q = run; q < ns * kSlab; ++q) {
-      const uint32_t ln = q / ns;
-      ent[t0 + ((int64_t)(q - ln * ns) << 5) + ln] = pad;
+    if (s == 0) {
+      const int64_t t0 = d.ts[b];
+      const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
+      for (uint32_t qq = run; qq < ns * kSlab; ++qq) {
+        const uint32_t ln = qq / ns;
+        ent[t0 + ((int64_t)(qq - ln * ns) << 5) + ln] = pad;
+      }
     }
   }
   __syncthreads();
   const uint32_t wmask = (1u << logW) - 1u;
   uint32_t* cw = d.cnt + warp * B;
   const uint32_t lt = (1u << lane) - 1u;
-  for (int r = warp; r < rows; r += kBanks) {
-    const int s = d.ps[r], e = d.ps[r + 1];
-    for (int k0 = s; k0 < e; k0 += 32) {
+  for (int r = q.r_lo + ((warp - q.r_lo) & (kBanks - 1)); r < q.r_hi; r += kBanks) {
+    const int s0 = d.ps[r - q.r_lo], e = d.ps[r - q.r_lo + 1];
+    for (int k0 = s0; k0 < e; k0 += 32) {
       const int k = k0 + lane;
       const uint32_t c = k < e ? (uint32_t)(int32_t)idx[k] : 0xFFFFFFFFu;
       uint32_t b = c >> logW;
@@ -429,11 +478,11 @@ __global__ void __launch_bounds__(kBuildThreads) panel_scatter_kernel(
       if (v && (peers & lt) == 0) cw[b] = base + __popc(peers);
       __syncwarp();
       if (v) {
-        const uint32_t q = base + __popc(peers & lt);
+        const uint32_t qq = base + __popc(peers & lt);
         const int64_t t0 = d.ts[b];
         const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
-        const uint32_t ln = q / ns;
-        ent[t0 + ((int64_t)(q - ln * ns) << 5) + ln] =
+        const uint32_t ln = qq / ns;
+        ent[t0 + ((int64_t)(qq - ln * ns) << 5) + ln] =
             make_uint2(((uint32_t)r << 16) | (c & wmask), __float_as_uint(lv));
       }
     }
@@ -454,14 +503,16 @@ static int build_tiles_direct(const int32_t* ptr, const IT* idx, const float* la
                               const TileGeom& g, const LayoutPtrs& L, void* ws, size_t ws_bytes,
                               cudaStream_t st) {
   const int64_t ntiles = (int64_t)g.P * g.B;
+  const int Rs = (int)ceil_div64(g.R, g.S);
   Carver cv(ws, ws_bytes);
-  uint32_t* cnt = cv.take<uint32_t>(ntiles * kBanks);
+  uint32_t* cnt = cv.take<uint32_t>(ntiles * g.S * kBanks);
   int64_t* stmp = cv.take<int64_t>(scan_tmp_elems(ntiles + 1));
   if (!cv.ok) {
     set_error("build_tiles: workspace too small");
     return kWorkspaceTooSmall;
   }
-  const size_t smem = direct_smem(g.R, g.B);
+  SINKSLOT_REQUIRE(g.P <= 65535, "build_tiles: too many panels");
+  const size_t smem = direct_smem(Rs, g.B);
   {
     // the dynamic shared-memory limit is a per-device function attribute
     static bool configured[64] = {};
@@ -477,14 +528,17 @@ static int build_tiles_direct(const int32_t* ptr, const IT* idx, const float* la
       if (dev >= 0 && dev < 64) configured[dev] = true;
     }
   }
+  const dim3 grid((unsigned)g.S, (unsigned)g.P);
   SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.header, 0, 8 * sizeof(int64_t), st));
-  panel_count_kernel<IT><<<(unsigned)g.P, kBuildThreads, smem, st>>>(
-      ptr, idx, g.nseg, g.R, g.B, g.logW, cnt, L.tstart,
+  panel_count_kernel<IT><<<grid, kBuildThreads, smem, st>>>(
+      ptr, idx, g.nseg, g.R, Rs, g.B, g.logW, cnt,
       reinterpret_cast<unsigned long long*>(L.header));
   SINKSLOT_CHECK_LAUNCH();
+  tile_size_kernel<<<grid_t(ntiles, 256), 256, 0, st>>>(cnt, ntiles, g.B, g.S, L.tstart);
+  SINKSLOT_CHECK_LAUNCH();
   SINKSLOT_TRY(scan_exclusive_i64(L.tstart, ntiles, stmp, L.tstart + ntiles, st));
-  panel_scatter_kernel<IT><<<(unsigned)g.P, kBuildThreads, smem, st>>>(
-      ptr, idx, lam, g.nseg, g.R, g.B, g.logW, cnt, L.tstart, L.ent);
+  panel_scatter_kernel<IT><<<grid, kBuildThreads, smem, st>>>(
+      ptr, idx, lam, g.nseg, g.R, Rs, g.B, g.logW, cnt, L.tstart, L.ent);
   SINKSLOT_CHECK_LAUNCH();
   fill_tail_kernel<<<grid_t(ntiles * (kSlab - 1) + 1, 256), 256, 0, st>>>(L.ent, L.tstart + ntiles,
                                                                           g.cap, g.R);

@@ -22,6 +22,7 @@ struct TileGeom {
   size_t layout_bytes = 0;  // header + tile_start + meta + lam
   size_t build_bytes = 0;   // scratch of the builder
   bool direct = false;      // built by the per-panel counting kernels (else by a sort)
+  int S = 1;                // sub-panels (CTAs) per panel of the direct builder
 };
 
 TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms);
