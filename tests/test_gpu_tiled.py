@@ -1,7 +1,8 @@
 """The shared-memory-staged (tiled) half-step against the exact kernel.
 
 The tiled pass stabilises each row's log-sum-exp by its previous value and sums
-in 64-bit fixed point; rows outside the safe window go to the exact kernel.
+in fixed point (2^-32 units, exact); rows outside the safe window go to the exact
+kernel.
 Checks: the layout holds exactly the CSR's entries, tile by tile; tiled and
 exact solves agree to the parity bar on several problems (uniform and
 Dirichlet weights, n != m, tiny and large eps so rows are handed back); tiled
@@ -59,7 +60,8 @@ def _align(x, a=256):
     return (x + a - 1) // a * a
 
 
-@pytest.mark.parametrize("n,m,L", [(3000, 2000, 16), (70000, 50000, 8), (300, 250, 40)])
+@pytest.mark.parametrize("n,m,L", [(3000, 2000, 16), (70000, 50000, 8), (300, 250, 40),
+                                   (2000, 6_500_000, 2)])  # 397 blocks: the sort-based builder
 def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     from sinkslot_b200.sinkhorn_solvers import build_tiles
     csr = _problem(n, m, 3, 1, "dirichlet", cuda, L=L)
