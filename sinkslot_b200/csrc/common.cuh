@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <utility>
 #include <stdint.h>
 
 #include <string>
@@ -110,6 +111,45 @@ __device__ __forceinline__ uint32_t nonneg_float_bits(float f) { return __float_
 template <typename T>
 __device__ __forceinline__ T ld_stream(const T* p) {
   return __ldcs(p);
+}
+
+// Programmatic dependent launch.  The solve loop's half-step kernels are
+// launched so that each may be scheduled before the one ahead of it has
+// finished (launch_chained below).  Every such kernel waits, before it reads or
+// writes anything, until the kernel before it has completed and its writes are
+// visible (chain_enter); as each waits for the one before, the completion of any
+// of them implies the completion of all earlier ones.  A block lets the next
+// kernel start launching once its main work is done (chain_release): released
+// at entry instead, the next grid's launch competed with the running one
+// (measured 4% slower per half-step; released late, 1.8% faster than no chaining).
+#ifndef SINKSLOT_PDL
+#define SINKSLOT_PDL 1
+#endif
+__device__ __forceinline__ void chain_enter() {
+#if SINKSLOT_PDL
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+#endif
+}
+__device__ __forceinline__ void chain_release() {
+#if SINKSLOT_PDL
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+#endif
+}
+
+template <typename... Params, typename... Args>
+static inline cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block,
+                                         size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = SINKSLOT_PDL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace sinkslot

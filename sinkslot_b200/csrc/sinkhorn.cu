@@ -116,8 +116,10 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     const float* self_old, float* out, int64_t nseg, float w_old, float w_new, float* prev,
     uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count,
     const PeerOut po, unsigned int* done) {
+  chain_enter();
   seg_pass<IT, G, OUT, CHK>(ptr, idx, lam, other, selfpot, base, self_old, out, nseg, w_old,
                             w_new, prev, acc, list, list_count, po);
+  chain_release();
   if (po.n > 0) {
     __syncthreads();
     peer_cta_done(po, done);
@@ -139,10 +141,12 @@ static unsigned launch_g(const HalfStep& h, int out_mode, int chk, cudaStream_t 
   const int64_t cap = (int64_t)num_sms() * (h.list ? 4 : 16);
   const unsigned grid = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
   const IT* idx = static_cast<const IT*>(h.idx);
-#define SINKSLOT_HS(OUTM, CHKM)                                                           \
-  half_step_kernel<IT, G, OUTM, CHKM><<<grid, kLseThreads, 0, st>>>(                      \
-      h.ptr, idx, h.lam, h.other, h.selfpot, h.base, h.self_old, h.out, h.nseg, h.w_old, h.w_new, \
-      h.prev, h.acc, h.list, h.list_count, h.peers, h.done)
+  // a failed launch leaves its error for SINKSLOT_CHECK_LAUNCH in half_step
+#define SINKSLOT_HS(OUTM, CHKM)                                                               \
+  (void)launch_chained(half_step_kernel<IT, G, OUTM, CHKM>, dim3(grid), dim3(kLseThreads), 0, \
+                       st, h.ptr, idx, h.lam, h.other, h.selfpot, h.base, h.self_old, h.out,  \
+                       h.nseg, h.w_old, h.w_new, h.prev, h.acc, h.list, h.list_count, h.peers, \
+                       h.done)
   if (out_mode == kOutPlain) {
     if (chk == kChkNone) SINKSLOT_HS(kOutPlain, kChkNone);
     else if (chk == kChkMarg) SINKSLOT_HS(kOutPlain, kChkMarg);

@@ -850,6 +850,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  chain_enter();
   // a pipeline wait of an earlier launch timed out: do nothing (the host reports it)
   if (*(volatile int*)a.err != 0) return;
   if (tid == 0) {
@@ -1007,6 +1008,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     }
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
   }
+  chain_release();
   check_reduce<CHK>(chk_bits, a.acc);
   if (a.peers.n > 0) {
     // consumers only: the producer warp stored no potential
@@ -1028,8 +1030,8 @@ static int launch_tiled(const TKArgs& a, size_t smem, cudaStream_t st) {
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   const int grid = std::min(a.P, num_sms());
-  tiled_half_step_kernel<OUT, CHK><<<grid, kPipeThreads, smem, st>>>(a);
-  SINKSLOT_CHECK_LAUNCH();
+  SINKSLOT_CUDA_TRY(launch_chained(tiled_half_step_kernel<OUT, CHK>, dim3(grid),
+                                   dim3(kPipeThreads), smem, st, a));
   return kOk;
 }
 
