@@ -136,10 +136,14 @@ int sinkslot_tiles_bytes(int64_t nseg, int64_t m_other, int64_t nnz, int64_t* la
  * Layout bytes: int64 header[8] | int64 tile_start[P*B + 1] | uint32
  * entries[cap][2] = {row within panel << 16 | column within block, lam bits},
  * each part 256-byte aligned; tile t = p*B + b holds entries [tile_start[t],
- * tile_start[t+1]), padded to a multiple of 32 with entries {R << 16, -inf}:
- * with the tile's entries stably sorted by (row within panel) mod 32 and N =
- * its padded count / 32, sorted position p is stored at slot 32*(p mod N) +
- * p / N; cap = nnz + 31*P*B. */
+ * tile_start[t+1]), padded with entries {R << 16, -inf} to 32 N entries, N
+ * odd: with the tile's entries stably sorted by (row within panel) mod 32 (the
+ * row bank), sorted position p is stored at slot 32*(p mod N) + p / N.  Inside
+ * each row-bank run [S, S + c) of a tile of at most 9216 entries the entries
+ * are then re-placed by column bank: the k-th entry (in run order) whose
+ * column mod 32 is t goes to position S + ((t - S) mod 32) + 32 k when that is
+ * below S + c, the others fill the remaining positions by class, then rank.
+ * cap = nnz + 63*P*B. */
 int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geom_host);
 
 /* Column-blocked layout of a CSR side for the shared-memory-staged half-step

@@ -100,6 +100,14 @@ constexpr int64_t kMaxTiledRow = 4096;
 constexpr long long kWaitCycles = 8000000000ll;  // ~4 s at 2 GHz: a wait this long is a bug
 
 constexpr int kSlab = 32;  // tiles are padded to whole warp slabs of entries
+// Slabs of a tile of n entries: ceil(n / 32), made odd (0 for an empty tile).
+// With N odd the lanes of a slab hold sorted positions q = lane * N + slab that
+// are distinct mod 32, which the column-bank placement (tile_colbank_kernel)
+// relies on.
+__host__ __device__ inline int64_t tile_slabs(int64_t n) {
+  const int64_t N = (n + kSlab - 1) / kSlab;
+  return N + (N > 0 && (N & 1) == 0 ? 1 : 0);
+}
 // slabs a consumer warp loads and processes together (its next tile's first
 // group is in flight while it works on the current tile)
 #ifndef SINKSLOT_TILE_GROUP
@@ -158,7 +166,7 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
   g.smem_bytes = pipe_smem((int)R, 1 << logW);
   const int64_t ntiles = (int64_t)g.P * g.B;
-  g.cap = nnz + (kSlab - 1) * ntiles;
+  g.cap = nnz + (2 * kSlab - 1) * ntiles;  // each tile: an odd number of slabs
   Carver cv(nullptr, 0);
   cv.take<int64_t>(8);            // header: [0] longest row of <= kMaxTiledRow entries
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
@@ -257,7 +265,7 @@ __global__ void tilekey_kernel(const uint32_t* __restrict__ rowid, const IT* __r
 }
 
 // ustart[t] = #{sorted keys of tiles < t}; cntp[t] = entries of tile t rounded
-// up to a slab (sorted keys are tile << kBankBits | bank)
+// up to an odd number of slabs (sorted keys are tile << kBankBits | bank)
 __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nnz, int64_t ntiles,
                                    int64_t* __restrict__ ustart, int64_t* __restrict__ cntp) {
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t <= ntiles;
@@ -273,7 +281,7 @@ __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nn
     };
     const int64_t s = lb(t);
     ustart[t] = s;
-    if (t < ntiles) cntp[t] = (lb(t + 1) - s + kSlab - 1) & ~int64_t(kSlab - 1);
+    if (t < ntiles) cntp[t] = tile_slabs(lb(t + 1) - s) * kSlab;
   }
 }
 
@@ -310,6 +318,8 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
     ent[pos] = make_uint2(((r % (uint32_t)R) << 16) | (c & wmask), __float_as_uint(lam[k]));
   }
 }
+
+static int place_column_banks(const TileGeom& g, const LayoutPtrs& L, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // direct builder: one CTA per sub-panel, no sort
@@ -398,7 +408,7 @@ __global__ void __launch_bounds__(kBuildThreads, 2) panel_count_kernel(
 }
 
 // tsize[t] = entries of tile t = p * B + b over its panel's S sub-panels and
-// the banks, rounded up to a slab
+// the banks, rounded up to an odd number of slabs
 __global__ void tile_size_kernel(const uint32_t* __restrict__ cnt, int64_t ntiles, int B, int S,
                                  int64_t* __restrict__ tsize) {
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ntiles;
@@ -407,7 +417,7 @@ __global__ void tile_size_kernel(const uint32_t* __restrict__ cnt, int64_t ntile
     const uint32_t* c = cnt + p * S * kBanks * B + b;
     uint32_t n = 0;
     for (int i = 0; i < S * kBanks; ++i) n += c[(int64_t)i * B];
-    tsize[t] = (int64_t)((n + kSlab - 1) & ~(uint32_t)(kSlab - 1));
+    tsize[t] = tile_slabs(n) * kSlab;
   }
 }
 
@@ -543,6 +553,147 @@ static int build_tiles_direct(const int32_t* ptr, const IT* idx, const float* la
   fill_tail_kernel<<<grid_t(ntiles * (kSlab - 1) + 1, 256), 256, 0, st>>>(L.ent, L.tstart + ntiles,
                                                                           g.cap, g.R);
   SINKSLOT_CHECK_LAUNCH();
+  return place_column_banks(g, L, st);
+}
+
+// ---------------------------------------------------------------------------
+// column-bank placement inside each row-bank run
+// ---------------------------------------------------------------------------
+// After the row-bank deal, a slab's 32 rows are in 32 different banks, but the
+// columns it gathers from the staged potential block fall in random banks
+// (~3.5 shared-memory wavefronts per gather).  Inside each row-bank run of a
+// tile (sorted positions [S, S + c)), the entries may be permuted freely; this
+// pass puts at sorted position q an entry whose column bank (column mod 32, the
+// bank of the staged potential) is q mod 32 wherever it can.  Lanes of a slab
+// hold positions q = lane * N + slab, distinct mod 32 for odd N, so entries
+// placed on target gather from 32 different banks.  In a run, the k-th entry of
+// column class t (in row-bank order) goes to relative position
+// ((t - S) mod 32) + 32 k when that is below c; the others fill the remaining
+// positions in a fixed order (classes ascending, then k), so the layout is
+// deterministic.  Tiles larger than kPlaceMax entries keep the row-bank order.
+// 16 warps per block, each placing two runs, and a 72 KB staging buffer plus an
+// 18 KB hole table: two blocks per SM.
+#ifndef SINKSLOT_TILE_COLBANK
+#define SINKSLOT_TILE_COLBANK 1
+#endif
+constexpr int kPlaceWarps = 16;
+constexpr int kPlaceThreads = 32 * kPlaceWarps;
+constexpr int kPlaceMax = 9216;
+constexpr size_t kPlaceSmem = (size_t)kPlaceMax * (sizeof(uint2) + sizeof(uint16_t));
+
+__global__ void __launch_bounds__(kPlaceThreads, 2) tile_colbank_kernel(
+    const int64_t* __restrict__ tstart, uint2* __restrict__ ent, int64_t ntiles, int R) {
+  extern __shared__ __align__(16) unsigned char place_sm[];
+  uint2* tbuf = reinterpret_cast<uint2*>(place_sm);  // the tile, by sorted position
+  // free relative positions of each run, run r's at [S_r, S_r + holes): a
+  // leftover entry reads its position with one load
+  uint16_t* hole = reinterpret_cast<uint16_t*>(place_sm + (size_t)kPlaceMax * sizeof(uint2));
+  __shared__ uint32_t ecnt[kBanks][33];   // per run: entries per column class
+  __shared__ uint32_t run_k[kBanks][32];  // per run: running rank per class
+  __shared__ uint32_t pre_o[kBanks][32];  // per run: leftover entries before class t
+  __shared__ uint32_t rstart[kBanks + 1];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t ts = tstart[t];
+    const int64_t len = tstart[t + 1] - ts;  // 32 N
+    if (len == 0 || len > kPlaceMax) continue;  // uniform over the block
+    const uint32_t N = (uint32_t)(len >> 5);
+    // slots in order (coalesced): slot 32 s + l holds sorted position l N + s
+    for (uint32_t q = tid; q < (uint32_t)len; q += kPlaceThreads)
+      tbuf[(q & 31u) * N + (q >> 5)] = ent[ts + q];
+    for (int i = tid; i < kBanks * 33; i += kPlaceThreads) (&ecnt[0][0])[i] = 0;
+    __syncthreads();
+    // entries per (row bank, column class), padding excluded
+    for (uint32_t q = tid; q < (uint32_t)len; q += kPlaceThreads) {
+      const uint32_t x = tbuf[q].x;
+      if ((x >> 16) < (uint32_t)R) atomicAdd(&ecnt[(x >> 16) & (kBanks - 1)][x & 31u], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t v = 0;
+      for (int u = 0; u < 32; ++u) v += ecnt[lane][u];
+      uint32_t incl = v;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t a = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += a;
+      }
+      rstart[lane] = incl - v;
+      if (lane == 31) rstart[kBanks] = incl;
+    }
+    __syncthreads();
+    // warp w: the runs of row banks w and w + kPlaceWarps
+    for (int rw = warp; rw < kBanks; rw += kPlaceWarps) {
+      const uint32_t S = rstart[rw], c = rstart[rw + 1] - S;
+      {
+        // lane = class t: positions of the class, matched entries, holes, leftovers
+        const uint32_t e_t = ecnt[rw][lane];
+        const uint32_t off = ((uint32_t)lane - S) & 31u;
+        const uint32_t p_t = c > off ? (c - 1 - off) / 32 + 1 : 0u;
+        const uint32_t m_t = e_t < p_t ? e_t : p_t;
+        const uint32_t h_t = p_t - m_t, o_t = e_t - m_t;
+        uint32_t ih = h_t, io = o_t;
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t a = __shfl_up_sync(0xffffffffu, ih, o);
+          const uint32_t b = __shfl_up_sync(0xffffffffu, io, o);
+          if (lane >= o) {
+            ih += a;
+            io += b;
+          }
+        }
+        // the class's free positions: ranks e_t .. p_t - 1
+        for (uint32_t i = 0; i < h_t; ++i)
+          hole[S + (ih - h_t) + i] = (uint16_t)(off + 32u * (e_t + i));
+        pre_o[rw][lane] = io - o_t;
+        run_k[rw][lane] = 0;
+      }
+      __syncwarp();
+      for (uint32_t j0 = 0; j0 < c; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        const bool v = j < c;
+        const uint2 e = v ? tbuf[S + j] : make_uint2(0u, 0u);
+        const uint32_t cls = v ? (e.x & 31u) : 32u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, cls);
+        const uint32_t base = v ? run_k[rw][cls] : 0u;
+        __syncwarp();
+        if (v && (peers & lt) == 0) run_k[rw][cls] = base + __popc(peers);
+        __syncwarp();
+        if (v) {
+          const uint32_t k = base + __popc(peers & lt);
+          const uint32_t off = (cls - S) & 31u;
+          const uint32_t p_c = c > off ? (c - 1 - off) / 32 + 1 : 0u;
+          // on target, or leftover number L into free position number L
+          const uint32_t jn = k < p_c ? off + 32u * k : (uint32_t)hole[S + pre_o[rw][cls] + (k - p_c)];
+          const uint32_t qn = S + jn;
+          const uint32_t ln = qn / N;
+          ent[ts + ((int64_t)(qn - ln * N) << 5) + ln] = e;
+        }
+      }
+    }
+    __syncthreads();  // the next tile reuses the buffers
+  }
+}
+
+static int place_column_banks(const TileGeom& g, const LayoutPtrs& L, cudaStream_t st) {
+#if SINKSLOT_TILE_COLBANK
+  const int64_t ntiles = (int64_t)g.P * g.B;
+  if (ntiles == 0 || g.nnz == 0) return kOk;
+  const size_t smem = kPlaceSmem;
+  static bool configured[64] = {};
+  int dev = 0;
+  SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(tile_colbank_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, 2 * (int64_t)num_sms());
+  tile_colbank_kernel<<<grid, kPlaceThreads, smem, st>>>(L.tstart, L.ent, ntiles, g.R);
+  SINKSLOT_CHECK_LAUNCH();
+#else
+  (void)g; (void)L; (void)st;
+#endif
   return kOk;
 }
 
@@ -612,7 +763,7 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
         skey, perm, rowid, static_cast<const int32_t*>(idx), lam, g.nnz, g.R, g.logW, ustart,
         L.tstart, L.ent);
   SINKSLOT_CHECK_LAUNCH();
-  return kOk;
+  return place_column_banks(g, L, st);
 }
 
 // ---------------------------------------------------------------------------

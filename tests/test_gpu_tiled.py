@@ -60,8 +60,58 @@ def _align(x, a=256):
     return (x + a - 1) // a * a
 
 
+def _column_bank_positions(p, tile, rb, cls, tile_len, place_max=9216):
+    """Sorted positions after the column-bank placement inside each row-bank run.
+
+    p: position of each entry in its tile's row-bank order; tile, rb, cls: its
+    tile, row bank and column class (column mod 32), all in that order.  In a run
+    [S, S + c), the k-th entry of class t (in run order) goes to relative position
+    ((t - S) mod 32) + 32 k when below c; the others fill the free positions by
+    class, then rank.  Tiles of more than place_max entries keep their order.
+    """
+    n = p.size
+    if n == 0:
+        return p
+    run = tile.astype(np.int64) * 32 + rb
+    start = np.r_[True, run[1:] != run[:-1]]
+    run_id = np.cumsum(start) - 1
+    S = p[start][run_id]
+    nrun = int(run_id[-1]) + 1
+    # rank of each entry among its run's entries of the same class, in run order
+    o2 = np.lexsort((p, cls, run_id))
+    g = run_id[o2] * 32 + cls[o2]
+    gstart = np.r_[True, g[1:] != g[:-1]]
+    first = np.maximum.accumulate(np.where(gstart, np.arange(n), 0))
+    k = np.empty(n, dtype=np.int64)
+    k[o2] = np.arange(n) - first
+    e_all = np.bincount(run_id * 32 + cls, minlength=nrun * 32).reshape(nrun, 32)
+    S_run = p[start]
+    c_run = np.bincount(run_id)
+    off_all = (np.arange(32)[None, :] - S_run[:, None]) % 32
+    p_all = np.where(c_run[:, None] > off_all, (c_run[:, None] - 1 - off_all) // 32 + 1, 0)
+    m_all = np.minimum(e_all, p_all)
+    h_all, o_all = p_all - m_all, e_all - m_all
+    pre_h = np.concatenate([np.zeros((nrun, 1), np.int64), np.cumsum(h_all, 1)], 1)
+    pre_o = np.concatenate([np.zeros((nrun, 1), np.int64), np.cumsum(o_all, 1)], 1)
+    off = (cls - S) % 32
+    pc = p_all[run_id, cls]
+    jn = off + 32 * k
+    left = np.nonzero(k >= pc)[0]
+    if left.size:
+        rl = run_id[left]
+        L = pre_o[rl, cls[left]] + (k[left] - pc[left])
+        u = (pre_h[rl, 1:32] <= L[:, None]).sum(1)  # the largest class u with pre_h[u] <= L
+        kk = e_all[rl, u] + (L - pre_h[rl, u])
+        jn[left] = (u - S[left]) % 32 + 32 * kk
+    out = S + jn
+    keep = tile_len > place_max
+    out[keep] = p[keep]
+    return out
+
+
 @pytest.mark.parametrize("n,m,L", [(3000, 2000, 16), (70000, 50000, 8), (300, 250, 40),
-                                   (2000, 6_500_000, 2)])  # 397 blocks: the sort-based builder
+                                   (2000, 6_500_000, 2),   # 397 blocks: the sort-based builder
+                                   (14800, 10000, 64)])    # tiles of ~12800: row-bank order kept
 def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     from sinkslot_b200.sinkhorn_solvers import build_tiles
     csr = _problem(n, m, 3, 1, "dirichlet", cuda, L=L)
@@ -71,7 +121,7 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     P, R, B, logW, smem = _geometry(n, m, nnz)
     assert smem <= 227 * 1024 and R < 65536 and P * R >= n and B << logW >= m
     T = P * B
-    cap = nnz + 31 * T
+    cap = nnz + 63 * T
     off = _align(64)
     tstart = layout[off:off + 8 * (T + 1)].view(np.int64)
     off = _align(off + 8 * (T + 1))
@@ -84,9 +134,12 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     row_of = np.repeat(np.arange(n), np.diff(ptr_h))
     tile_of = (row_of // R) * B + (idx_h >> logW)
     # inside a tile: stably by the bank of the row state, (row within panel) mod 32
-    order = np.lexsort((np.arange(nnz), (row_of % R) % 32, tile_of))
+    rb_all = (row_of % R) % 32
+    order = np.lexsort((np.arange(nnz), rb_all, tile_of))
     counts = np.bincount(tile_of, minlength=T)
-    padded = (counts + 31) // 32 * 32
+    slabs = (counts + 31) // 32
+    slabs += (slabs > 0) & (slabs % 2 == 0)  # an odd number of slabs
+    padded = slabs * 32
     np.testing.assert_array_equal(tstart, np.concatenate([[0], np.cumsum(padded)]))
     # padding: the dummy row R, column 0, lam = -inf
     want_meta = np.full(cap, R << 16, dtype=np.uint64)
@@ -94,6 +147,7 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     ustart = np.concatenate([[0], np.cumsum(counts)])
     t_o = tile_of[order]
     p = np.arange(nnz) - ustart[t_o]
+    p = _column_bank_positions(p, t_o, rb_all[order], idx_h[order] & 31, padded[t_o])
     ns = padded[t_o] // 32
     # sorted position p of a tile with N slabs: slab p mod N, lane p // N
     pos = tstart[t_o] + 32 * (p % ns) + p // ns
