@@ -363,6 +363,27 @@ __device__ __forceinline__ SubRows sub_rows(int64_t nseg, int R, int Rs) {
   return q;
 }
 
+// A warp's walk over the 32-entry chunks of its rows r = r_first, r_first + 32,
+// ... < r_hi (panel-local; offsets in ps, indexed from r_lo).  next_chunk moves
+// to the next non-empty chunk; the state starts one row before r_first.
+struct ChunkWalk {
+  int r, k0, e;
+};
+
+__device__ __forceinline__ bool next_chunk(const int32_t* ps, int r_lo, int r_hi, ChunkWalk& w) {
+  if (w.k0 + 32 < w.e) {
+    w.k0 += 32;
+    return true;
+  }
+  do {
+    w.r += kBanks;
+    if (w.r >= r_hi) return false;
+    w.k0 = ps[w.r - r_lo];
+    w.e = ps[w.r - r_lo + 1];
+  } while (w.k0 >= w.e);
+  return true;
+}
+
 // Per sub-panel (blockIdx.x of gridDim.x, panel blockIdx.y): entries per
 // (bank, block) into cnt_out[(p * S + s) * kBanks + bank][block], and the
 // longest row of at most kMaxTiledRow entries into *longest.
@@ -390,17 +411,25 @@ __global__ void __launch_bounds__(kBuildThreads, 2) panel_count_kernel(
   if (lane == 0 && best > 0) atomicMax(longest, best);
   uint32_t* cw = d.cnt + warp * B;
   const uint32_t lt = (1u << lane) - 1u;
-  for (int r = q.r_lo + ((warp - q.r_lo) & (kBanks - 1)); r < q.r_hi; r += kBanks) {
-    const int s = d.ps[r - q.r_lo], e = d.ps[r - q.r_lo + 1];
-    for (int k0 = s; k0 < e; k0 += 32) {
-      const int k = k0 + lane;
-      uint32_t b = k < e ? ((uint32_t)(int32_t)idx[k] >> logW) : 0xFFFFFFFFu;
-      const bool v = b < (uint32_t)B;  // an index outside [0, m_other) is left out
-      if (!v) b = 0xFFFFFFFFu;
-      const uint32_t peers = __match_any_sync(0xffffffffu, b);
-      if (v && (peers & lt) == 0) cw[b] += __popc(peers);
-      __syncwarp();
-    }
+  // chunks of the warp's rows, each one's indices loaded a chunk ahead
+  ChunkWalk cur{q.r_lo + ((warp - q.r_lo) & (kBanks - 1)) - kBanks, 0, 0};
+  bool have = next_chunk(d.ps, q.r_lo, q.r_hi, cur);
+  uint32_t c_cur = have && cur.k0 + lane < cur.e ? (uint32_t)(int32_t)idx[cur.k0 + lane]
+                                                 : 0xFFFFFFFFu;
+  while (have) {
+    ChunkWalk nxt = cur;
+    const bool have_n = next_chunk(d.ps, q.r_lo, q.r_hi, nxt);
+    const uint32_t c_n = have_n && nxt.k0 + lane < nxt.e
+                             ? (uint32_t)(int32_t)idx[nxt.k0 + lane] : 0xFFFFFFFFu;
+    uint32_t b = c_cur >> logW;  // past the row's end: 0xFFFFFFFF >> logW >= B
+    const bool v = b < (uint32_t)B;  // an index outside [0, m_other) is left out
+    if (!v) b = 0xFFFFFFFFu;
+    const uint32_t peers = __match_any_sync(0xffffffffu, b);
+    if (v && (peers & lt) == 0) cw[b] += __popc(peers);
+    __syncwarp();
+    cur = nxt;
+    c_cur = c_n;
+    have = have_n;
   }
   __syncthreads();
   uint32_t* co = cnt_out + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * kBanks * B;
@@ -473,29 +502,45 @@ __global__ void __launch_bounds__(kBuildThreads, 1) panel_scatter_kernel(
   const uint32_t wmask = (1u << logW) - 1u;
   uint32_t* cw = d.cnt + warp * B;
   const uint32_t lt = (1u << lane) - 1u;
-  for (int r = q.r_lo + ((warp - q.r_lo) & (kBanks - 1)); r < q.r_hi; r += kBanks) {
-    const int s0 = d.ps[r - q.r_lo], e = d.ps[r - q.r_lo + 1];
-    for (int k0 = s0; k0 < e; k0 += 32) {
-      const int k = k0 + lane;
-      const uint32_t c = k < e ? (uint32_t)(int32_t)idx[k] : 0xFFFFFFFFu;
-      uint32_t b = c >> logW;
-      const bool v = k < e && b < (uint32_t)B;  // as in panel_count_kernel
-      if (!v) b = 0xFFFFFFFFu;
-      const float lv = v ? lam[k] : 0.0f;
-      const uint32_t peers = __match_any_sync(0xffffffffu, b);
-      const uint32_t base = v ? cw[b] : 0u;
-      __syncwarp();
-      if (v && (peers & lt) == 0) cw[b] = base + __popc(peers);
-      __syncwarp();
-      if (v) {
-        const uint32_t qq = base + __popc(peers & lt);
-        const int64_t t0 = d.ts[b];
-        const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
-        const uint32_t ln = qq / ns;
-        ent[t0 + ((int64_t)(qq - ln * ns) << 5) + ln] =
-            make_uint2(((uint32_t)r << 16) | (c & wmask), __float_as_uint(lv));
-      }
+  // chunks of the warp's rows, each one's entries loaded a chunk ahead
+  ChunkWalk cur{q.r_lo + ((warp - q.r_lo) & (kBanks - 1)) - kBanks, 0, 0};
+  bool have = next_chunk(d.ps, q.r_lo, q.r_hi, cur);
+  uint32_t c_cur = 0xFFFFFFFFu;
+  float l_cur = 0.0f;
+  if (have && cur.k0 + lane < cur.e) {
+    c_cur = (uint32_t)(int32_t)idx[cur.k0 + lane];
+    l_cur = lam[cur.k0 + lane];
+  }
+  while (have) {
+    ChunkWalk nxt = cur;
+    const bool have_n = next_chunk(d.ps, q.r_lo, q.r_hi, nxt);
+    uint32_t c_n = 0xFFFFFFFFu;
+    float l_n = 0.0f;
+    if (have_n && nxt.k0 + lane < nxt.e) {
+      c_n = (uint32_t)(int32_t)idx[nxt.k0 + lane];
+      l_n = lam[nxt.k0 + lane];
     }
+    const uint32_t c = c_cur;
+    uint32_t b = c >> logW;
+    const bool v = cur.k0 + lane < cur.e && b < (uint32_t)B;  // as in panel_count_kernel
+    if (!v) b = 0xFFFFFFFFu;
+    const uint32_t peers = __match_any_sync(0xffffffffu, b);
+    const uint32_t base = v ? cw[b] : 0u;
+    __syncwarp();
+    if (v && (peers & lt) == 0) cw[b] = base + __popc(peers);
+    __syncwarp();
+    if (v) {
+      const uint32_t qq = base + __popc(peers & lt);
+      const int64_t t0 = d.ts[b];
+      const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
+      const uint32_t ln = qq / ns;
+      ent[t0 + ((int64_t)(qq - ln * ns) << 5) + ln] =
+          make_uint2(((uint32_t)cur.r << 16) | (c & wmask), __float_as_uint(l_cur));
+    }
+    cur = nxt;
+    c_cur = c_n;
+    l_cur = l_n;
+    have = have_n;
   }
 }
 
