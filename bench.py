@@ -386,6 +386,8 @@ def run_b200_sharded(args, world, rank, local):
     t_half = ms / 1e3 / (2 * args.steps)
     # this rank's bytes per half-step: its slice's entries and segments
     r_nnz, c_nnz = solver.row[3], solver.col[3]
+    sides = {"row": "tiled" if solver.r_tiles is not None else "exact",
+             "col": "tiled" if solver.c_tiles is not None else "exact"}
     bytes_row = r_nnz * (solver.row[1].element_size() + 4) + 16 * solver.nr
     bytes_col = c_nnz * (solver.col[1].element_size() + 4) + 16 * solver.nc
     achieved = max_over_ranks(-((bytes_row + bytes_col) / (2 * t_half) / 1e9), world, dev)
@@ -442,8 +444,11 @@ def run_b200_sharded(args, world, rank, local):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": peak_kind, "traffic": None,
-                         "kernel": "per rank: tiled_half_step_kernel + exact pass + peer push "
-                                   "+ epoch wait, per half-step, averaged over the timed region",
+                         "kernel": "per rank: the half-step kernel of each side (tiled "
+                                   "half-step + exact pass over handed-back rows, or the "
+                                   "exact kernel) + peer push + epoch wait, per half-step, "
+                                   "averaged over the timed region",
+                         "sides": sides,
                          "bytes_per_half_step_rank0": {"row": bytes_row, "col": bytes_col},
                          "half_step_us": round(t_half * 1e6, 2)},
             "cpu_baseline": None,
