@@ -197,8 +197,9 @@ constexpr size_t scatter_smem() {
 
 // Occupancy of the scatter pass, which is latency-bound (one tile per block):
 // registers bounded for 5 blocks per SM (4 with 12-byte key/value pairs, which
-// would spill at 5) and the whole shared-memory carveout (measured: the 16 passes
-// of a 2^20 set-up 11.6 -> 9.2 ms against the defaults).
+// would spill at 5) and the whole shared-memory carveout (measured at 2^20: the
+// first set-up's 16 passes 11.6 -> 9.2 ms against the defaults; a warm set-up's
+// stay at ~9.3 ms).
 #ifndef SINKSLOT_SORT_MIN_BLOCKS
 #define SINKSLOT_SORT_MIN_BLOCKS 5
 #endif
