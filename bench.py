@@ -64,13 +64,76 @@ def ncu_traffic():
 
 
 def make_inputs(rank: int, w=None):
+    """x, y, a, b on the host for workload w: drawn in that order from torch's
+    global CPU generator seeded with the workload's seed (+1000 per replica)."""
     w = WORKLOAD if w is None else w
     torch.manual_seed(w["data_seed"] + 1000 * rank)
-    x = torch.randn(w["n"], w["d"])
-    y = torch.randn(w["m"], w["d"]) + w["shift"]
-    a = torch.full((w["n"],), 1.0 / w["n"])
-    b = torch.full((w["m"],), 1.0 / w["m"])
+    gen = w.get("gen", "gauss")
+    n, m, d = w["n"], w["m"], w["d"]
+    if gen == "gauss":
+        x = torch.randn(n, d)
+        y = torch.randn(m, d) + w["shift"]
+    elif gen == "gmm_unit":
+        x = gmm_unit_cloud(n, w["components"], d, w["std"])
+        y = gmm_unit_cloud(m, w["components"], d, w["std"])
+    elif gen == "gmm_shift":
+        means = w["spread"] * torch.randn(w["components"], d)
+        x = means[torch.randint(0, w["components"], (n,))] + torch.randn(n, d)
+        y = means[torch.randint(0, w["components"], (m,))] + torch.randn(m, d) + w["shift"]
+    else:
+        raise ValueError(gen)
+    if w.get("weights", "uniform") == "dirichlet":
+        a = -torch.rand(n).clamp_min(1e-12).log()
+        b = -torch.rand(m).clamp_min(1e-12).log()
+        a, b = a / a.sum(), b / b.sum()
+    else:
+        a = torch.full((n,), 1.0 / n)
+        b = torch.full((m,), 1.0 / m)
     return x, y, a, b
+
+
+def gmm_unit_cloud(n: int, k: int, d: int, std: float) -> torch.Tensor:
+    """n points of a k-component Gaussian mixture in [0, 1]^d: means uniform in
+    the cube, isotropic std, clipped to the cube (a colour cloud's shape)."""
+    means = torch.rand(k, d)
+    comp = torch.randint(0, k, (n,))
+    return (means[comp] + std * torch.randn(n, d)).clamp_(0.0, 1.0)
+
+
+# The other workloads of the benchmark suite (one JSON line each, --config):
+#   cfg3  colour-transfer shape: N = 2^21 source, M = 2^20 target RGB-like clouds,
+#         16-component mixtures in [0,1]^3 (std 0.05, clipped), Dirichlet(1)
+#         weights, eps = 0.005, L = 128, symmetric (alpha 0.5), marginal stop at
+#         1e-6 checked every 5 iterations; then the plan and the barycentric map
+#   cfg4  gradient flow: N = M = 2^18, d = 2, y ~ N(0, I) + 3 (seed 2), 200 outer
+#         steps x -= 0.1 * slot_grad(x, y, eps=0.01, L=100, seed=0, n_iters=200),
+#         the support rebuilt every step
+#   cfg5  scale-out: N = M = 2^24, d = 3, a 4-component Gaussian mixture (means
+#         2 * N(0, I), unit components; seed 3) against the same mixture shifted
+#         by 1.5; eps = 0.01, L = 64, 300 alternating iterations; under
+#         torch.distributed.run the fixed problem is partitioned over the ranks
+#         (strong scaling)
+CONFIGS = {
+    "cfg2": WORKLOAD,
+    "cfg3": dict(n=1 << 21, m=1 << 20, d=3, L=128, eps=0.005, n_iters=20000, data_seed=4,
+                 gen="gmm_unit", components=16, std=0.05, weights="dirichlet", proj_seed=0,
+                 variant="symmetric", alpha=0.5, stop_mode="marginal", stop_tol=1e-6,
+                 stop_check_every=5),
+    "cfg4": dict(n=1 << 18, m=1 << 18, d=2, L=100, eps=0.01, n_iters=200, data_seed=2,
+                 shift=3.0, proj_seed=0, outer_steps=200, lr=0.1, variant="alternating"),
+    "cfg5": dict(n=1 << 24, m=1 << 24, d=3, L=64, eps=0.01, n_iters=300, data_seed=3,
+                 gen="gmm_shift", components=4, spread=2.0, shift=1.5, proj_seed=0,
+                 variant="alternating"),
+}
+CONFIG_NAMES = {
+    "cfg3": "sinkslot colour-transfer shape, N=2^21 x M=2^20, d=3, 16-component mixtures in "
+            "[0,1]^3, Dirichlet weights, L=128, eps=0.005, symmetric, marginal stop 1e-6/5 "
+            "(seed 4); then plan + barycentric map",
+    "cfg4": "sinkslot gradient flow, N=M=2^18, d=2, y~N(0,I)+3 (seed 2), x -= 0.1*slot_grad("
+            "eps=0.01, L=100, 200 iterations), support rebuilt every step",
+    "cfg5": "sinkslot scale-out, N=M=2^24, d=3, 4-component mixture vs shifted mixture (seed 3), "
+            "L=64, eps=0.01, 300 alternating iterations",
+}
 
 
 # --------------------------------------------------------------------------
@@ -299,6 +362,11 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_from_support(rows, cols, lam, log_a, log_b, w)
+    triton_ref = None
+    if rank == 0 and world == 1 and not args.no_triton:
+        del rows, cols, lam, csr, r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, tiles
+        torch.cuda.empty_cache()
+        triton_ref = triton_reference_leg(X, Y, A, B, w, min(args.steps, 1000), value)
 
     if rank == 0:
         line = {
@@ -328,12 +396,14 @@ def run_b200(args):
                                              "col": round(t_col * 1e6, 2),
                                              "timing": "each launch alone, median of %d" % reps}},
             "cpu_baseline": cpu,
+            "triton_reference": triton_ref,
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "step": "sinkslot_solve(...) from pinned host x, y, a, b: support build + "
                             "%d iterations + potentials back" % w["n_iters"]},
-            # first iteration: 2 exact launches; later ones: tiled + exact pass per side
-            "gpu_launches": 2 * args.steps if args.plain else 2 + 4 * (args.steps - 1),
+            # first iteration: the row side's exact launch, the column side's max pass,
+            # tiled pass and exact pass; later ones: tiled + exact pass per side
+            "gpu_launches": 2 * args.steps if args.plain else 4 * args.steps,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -464,6 +534,396 @@ def run_b200_sharded(args, world, rank, local):
     dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------
+# the other workloads (--config cfg3 | cfg4 | cfg5), one GPU unless noted
+# --------------------------------------------------------------------------
+def _timed(stream, fn):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    out = fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return out, e0.elapsed_time(e1)
+
+
+def _side_bytes(idx, nnz, nseg):
+    return nnz * (idx.element_size() + 4) + 16 * nseg
+
+
+def _base_line(cfg, w, value, unit, world, steps, warmup, ms_per_step, clocks, extra_config):
+    config = {"workload": CONFIG_NAMES[cfg], "n": w["n"], "m": w["m"], "d": w["d"], "L": w["L"],
+              "eps": w["eps"]}
+    config.update(extra_config)
+    return {"metric": METRICS[cfg], "value": round(value, 3), "unit": unit, "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "strong" if cfg == "cfg5" else "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+            "clocks": clocks}
+
+
+METRICS = {
+    "cfg3": "colour-transfer-shaped solve: symmetric Sinkhorn iter/s at N=2^21,M=2^20,d=3,L=128 "
+            "fp32 (marginal stop)",
+    "cfg4": "gradient-flow outer steps/s at N=M=2^18,d=2,L=100 fp32 (support rebuilt per step)",
+    "cfg5": "Sinkhorn iter/s at N=M=2^24,d=3,L=64 fp32, rows/cols partitioned over the GPUs",
+}
+
+
+def run_cfg3(args):
+    """The colour-transfer shape: build, symmetric solve to the marginal stop,
+    plan export and barycentric map.  A step is one whole solve from zero
+    potentials; the value counts Sinkhorn iterations per second over the
+    timed solves (each check adds the reference's two check half-steps)."""
+    from types import SimpleNamespace
+    import sinkslot_b200
+    from sinkslot_b200 import sparse_barycentric_map, sparse_transport_plan
+    from sinkslot_b200.sinkhorn_solvers import build_tiles, sinkslot_symmetric_b200, tiles_pay_off
+    from sinkslot_b200.solver import _to_csr, cost_and_lam, sot_plan_coo
+
+    world, rank, local = dist_setup(1)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sinkslot_b200.load_library()
+    w = CONFIGS["cfg3"]
+    n, m = w["n"], w["m"]
+    x, y, a, b = make_inputs(0, w)
+    X, Y, A, B = (t.to(dev) for t in (x, y, a, b))
+    stream = torch.cuda.current_stream(dev)
+
+    def setup():
+        rows, cols, S = sot_plan_coo(X, Y, A, B, L=w["L"], seed=w["proj_seed"])
+        lam, _ = cost_and_lam(X, Y, rows, cols, S, w["eps"])
+        r = _to_csr(rows, cols, lam, n, want_perm=False)
+        c = _to_csr(cols, rows, lam, m, want_perm=False)
+        nnz = int(rows.numel())
+        tiles = (build_tiles(r[0], r[1], r[2], n, m) if tiles_pay_off(n, m, nnz) else None,
+                 build_tiles(c[0], c[1], c[2], m, n) if tiles_pay_off(m, n, nnz) else None)
+        return nnz, (r[0], r[1], r[2], c[0], c[1], c[2], A.log(), B.log(), n, m), tiles
+
+    (nnz, csr, tiles), setup_cold = _timed(stream, setup)
+    del nnz, csr, tiles
+    (nnz, csr, tiles), setup_ms = _timed(stream, setup)
+    stop = SimpleNamespace(mode=w["stop_mode"], max_iter=w["n_iters"], tol=w["stop_tol"],
+                           check_every=w["stop_check_every"])
+
+    def solve(st=stop):
+        return sinkslot_symmetric_b200(*csr, 0, st, eps=w["eps"], alpha=w["alpha"],
+                                       tiles=tiles)
+
+    # warm-up: a short solve (the full one runs to max_iter: tiny Dirichlet
+    # weights leave empty rows whose +inf potentials make every marginal check
+    # NaN, in the reference as here)
+    solve(SimpleNamespace(mode=stop.mode, max_iter=max(args.warmup, 3) * 5, tol=stop.tol,
+                          check_every=stop.check_every))
+    K = 1
+    sampler = ClockSampler(local)
+    sampler.start()
+    res, ms = _timed(stream, lambda: [solve() for _ in range(K)])
+    clocks = sampler.stop()
+    iters = sum(r[2] for r in res)
+    it, conv, viol = res[-1][2], res[-1][3], res[-1][4]
+    value = iters / (ms / 1e3)
+    checks = iters // w["stop_check_every"]
+    half_steps = 2 * iters + 2 * checks  # each check: both check-only half-steps
+    b_row, b_col = _side_bytes(csr[1], nnz, n), _side_bytes(csr[4], nnz, m)
+    achieved = (iters + checks) * (b_row + b_col) / (ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+
+    # end to end: sparse_transport_plan + sparse_barycentric_map from pinned host
+    # inputs, the barycentric images back to the host
+    xh, yh, ah, bh = (t.pin_memory() for t in (x, y, a, b))
+    txh = torch.empty(n, 3).pin_memory()
+
+    def e2e():
+        Xd, Yd = xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True)
+        Ad, Bd = ah.to(dev, non_blocking=True), bh.to(dev, non_blocking=True)
+        P = sparse_transport_plan(Xd, Yd, Ad, Bd, eps=w["eps"], L=w["L"], seed=w["proj_seed"],
+                                  stop_mode=w["stop_mode"], stop_max_iter=w["n_iters"],
+                                  stop_tol=w["stop_tol"],
+                                  stop_check_every=w["stop_check_every"], variant="symmetric",
+                                  alpha=w["alpha"])
+        Tx, _ = sparse_barycentric_map(P, Xd, Yd)
+        txh.copy_(Tx, non_blocking=True)
+
+    _, e2e_ms = _timed(stream, e2e)  # the solve above warmed the kernels and the allocator
+    line = _base_line("cfg3", w, value, UNIT, 1, K, 1, ms / K, clocks, {
+        "nnz": nnz, "iters_per_solve": it, "converged": bool(conv),
+        "final_viol": None if viol != viol else viol,
+        "setup_ms": round(setup_ms, 1), "setup_cold_ms": round(setup_cold, 1),
+        "step": "one symmetric solve from zero potentials to the marginal stop",
+        "sides": {"row": "tiled" if tiles[0] is not None else "exact",
+                  "col": "tiled" if tiles[1] is not None else "exact"},
+        "l2": "inputs larger than L2: %.2f GB of CSR+CSC streamed per iteration"
+              % ((b_row + b_col) / 1e9)})
+    line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                        "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                        "traffic": None, "half_steps_per_solve": half_steps // K if K else None,
+                        "kernel": "all half-steps of the timed solves (tiled + exact passes), "
+                                  "algorithmic bytes of each over the solve time"}
+    line["cpu_baseline"] = None
+    line["e2e"] = {"value": round(it / (e2e_ms / 1e3), 3), "unit": UNIT,
+                   "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (x, y, a, b)),
+                   "d2h_bytes_per_step": n * 3 * 4,
+                   "step": "sparse_transport_plan(symmetric, marginal stop) + "
+                           "sparse_barycentric_map from pinned host inputs, Tx back",
+                   "ms": round(e2e_ms, 1)}
+    line["gpu_launches"] = None
+    print(json.dumps(line), flush=True)
+
+
+def run_cfg4(args):
+    """Gradient flow: x -= lr * slot_grad(x, y, ...) with the support rebuilt
+    every step.  A step is one outer step; K = min(--steps, 200) steps timed."""
+    import sinkslot_b200
+    from sinkslot_b200 import slot_grad
+
+    world, rank, local = dist_setup(1)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sinkslot_b200.load_library()
+    w = CONFIGS["cfg4"]
+    x, y, a, b = make_inputs(0, w)
+    X0, Y, A, B = (t.to(dev) for t in (x, y, a, b))
+    stream = torch.cuda.current_stream(dev)
+
+    def step(X):
+        g = slot_grad(X, Y, A, B, w["eps"], w["L"], w["proj_seed"], w["n_iters"])
+        X.sub_(w["lr"] * g)
+
+    Xw = X0.clone()
+    for _ in range(max(args.warmup, 3)):
+        step(Xw)
+    K = max(1, min(args.steps, w["outer_steps"]))
+    X = X0.clone()
+    sampler = ClockSampler(local)
+    sampler.start()
+    _, ms = _timed(stream, lambda: [step(X) for _ in range(K)])
+    clocks = sampler.stop()
+    value = K / (ms / 1e3)
+    # one instrumented step: set-up, solve loop and export separately
+    parts = cfg4_breakdown(X0, Y, A, B, w, stream)
+    # end to end: every step copies x from pinned host memory and x back
+    xh = x.clone().pin_memory()
+    Yh, Ah, Bh = (t.pin_memory() for t in (y, a, b))
+    Yd, Ad, Bd = Yh.to(dev), Ah.to(dev), Bh.to(dev)
+
+    def e2e():
+        for _ in range(K):
+            Xd = xh.to(dev, non_blocking=True)
+            g = slot_grad(Xd, Yd, Ad, Bd, w["eps"], w["L"], w["proj_seed"], w["n_iters"])
+            Xd.sub_(w["lr"] * g)
+            xh.copy_(Xd, non_blocking=True)
+
+    _, e2e_ms = _timed(stream, e2e)
+    line = _base_line("cfg4", w, value, "steps/s", 1, K, max(args.warmup, 3), ms / K, clocks,
+                      {"outer_steps_timed": K, "lr": w["lr"], "n_iters": w["n_iters"],
+                       "per_step_ms": parts,
+                       "step": "slot_grad (support build + 200 alternating iterations + "
+                               "barycentric gradient) and the update x -= 0.1 grad"})
+    line["roofline"] = parts.pop("roofline")
+    line["cpu_baseline"] = None
+    line["e2e"] = {"value": round(K / (e2e_ms / 1e3), 3), "unit": "steps/s",
+                   "h2d_bytes_per_step": x.numel() * 4, "d2h_bytes_per_step": x.numel() * 4,
+                   "step": "x from pinned host, slot_grad, update, x back"}
+    line["gpu_launches"] = None
+    print(json.dumps(line), flush=True)
+
+
+def cfg4_breakdown(X, Y, A, B, w, stream):
+    """Milliseconds of one gradient-flow step's parts, and the roofline of its
+    solve loop (algorithmic bytes per iteration over the loop's time)."""
+    from sinkslot_b200.gradient import grad_from_plan
+    from sinkslot_b200.sinkhorn_solvers import (build_tiles, plan_values,
+                                                sinkslot_alternating_b200, tiles_pay_off)
+    from sinkslot_b200.solver import _to_csr, cost_and_lam, sot_plan_coo
+    n, m = w["n"], w["m"]
+    (rows, cols, S), t_sup = _timed(stream, lambda: sot_plan_coo(X, Y, A, B, L=w["L"],
+                                                                  seed=w["proj_seed"]))
+
+    def prep():
+        lam, _ = cost_and_lam(X, Y, rows, cols, S, w["eps"])
+        r = _to_csr(rows, cols, lam, n, want_perm=False)
+        c = _to_csr(cols, rows, lam, m, want_perm=False)
+        nnz = rows.numel()
+        tl = (build_tiles(r[0], r[1], r[2], n, m) if tiles_pay_off(n, m, nnz) else None,
+              build_tiles(c[0], c[1], c[2], m, n) if tiles_pay_off(m, n, nnz) else None)
+        return r, c, tl
+
+    (r, c, tl), t_prep = _timed(stream, prep)
+    csr = (r[0], r[1], r[2], c[0], c[1], c[2], A.log(), B.log(), n, m)
+    (phi, psi, *_), t_loop = _timed(stream, lambda: sinkslot_alternating_b200(
+        *csr, w["n_iters"], tiles=tl))
+    _, t_exp = _timed(stream, lambda: grad_from_plan(plan_values(
+        phi, psi, rows, cols, S, X, Y, w["eps"], grad_form=True), rows, cols, X, Y, A))
+    nnz = int(rows.numel())
+    b_iter = _side_bytes(r[1], nnz, n) + _side_bytes(c[1], nnz, m)
+    achieved = b_iter * w["n_iters"] / (t_loop / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    return {"support": round(t_sup, 3), "cost_csr_tiles": round(t_prep, 3),
+            "solve_loop": round(t_loop, 3), "plan_and_gradient": round(t_exp, 3), "nnz": nnz,
+            "sides": {"row": "tiled" if tl[0] is not None else "exact",
+                      "col": "tiled" if tl[1] is not None else "exact"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": peak_kind, "traffic": None,
+                         "kernel": "the solve loop of one outer step (200 iterations)"}}
+
+
+def run_cfg5(args):
+    """N = M = 2^24.  One GPU: the whole solve.  Under torch.distributed.run the
+    same fixed problem is partitioned over the ranks (strong scaling).  Fixed
+    iterations; K = min(--steps, 300) timed after the warm-up."""
+    import sinkslot_b200
+    from sinkslot_b200.sinkhorn_solvers import build_tiles, sinkslot_alternating_b200, tiles_pay_off
+    from sinkslot_b200.solver import _to_csr, cost_and_lam, sot_plan_coo
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sinkslot_b200.load_library()
+    w = CONFIGS["cfg5"]
+    n, m = w["n"], w["m"]
+    x, y, a, b = make_inputs(0, w)
+    X, Y, A, B = (t.to(dev) for t in (x, y, a, b))
+    stream = torch.cuda.current_stream(dev)
+    K = max(1, min(args.steps, w["n_iters"]))
+    peak, peak_kind = measured_peak_gbs()
+    if world == 1:
+        def setup():
+            rows, cols, S = sot_plan_coo(X, Y, A, B, L=w["L"], seed=w["proj_seed"], chunk=8)
+            lam, _ = cost_and_lam(X, Y, rows, cols, S, w["eps"])
+            del S
+            nnz = int(rows.numel())
+            r = _to_csr(rows, cols, lam, n, want_perm=False)
+            c = _to_csr(cols, rows, lam, m, want_perm=False)
+            del rows, cols, lam
+            tl = (build_tiles(r[0], r[1], r[2], n, m) if tiles_pay_off(n, m, nnz) else None,
+                  build_tiles(c[0], c[1], c[2], m, n) if tiles_pay_off(m, n, nnz) else None)
+            return nnz, (r[0], r[1], r[2], c[0], c[1], c[2], A.log(), B.log(), n, m), tl
+
+        (nnz, csr, tl), setup_ms = _timed(stream, setup)
+        sinkslot_alternating_b200(*csr, max(args.warmup, 3), tiles=tl)
+        sampler = ClockSampler(local)
+        sampler.start()
+        _, ms = _timed(stream, lambda: sinkslot_alternating_b200(*csr, K, tiles=tl))
+        clocks = sampler.stop()
+        b_iter = _side_bytes(csr[1], nnz, n) + _side_bytes(csr[4], nnz, m)
+        sides = {"row": "tiled" if tl[0] is not None else "exact",
+                 "col": "tiled" if tl[1] is not None else "exact"}
+        achieved = b_iter * K / (ms / 1e3) / 1e9
+    else:
+        from sinkslot_b200.sharded import ShardedSolver
+        (solver), setup_ms = _timed(stream, lambda: ShardedSolver(
+            X, Y, A, B, w["eps"], L=w["L"], seed=w["proj_seed"], chunk=8))
+        nnz = int(solver.rows.numel())
+        solver.solve(max(args.warmup, 3), copy_out=False)
+        sampler = ClockSampler(local) if rank == 0 else None
+        if sampler:
+            sampler.start()
+        barrier(world)
+        _, ms = _timed(stream, lambda: solver.solve(K, copy_out=False))
+        barrier(world)
+        clocks = sampler.stop() if sampler else None
+        ms = max_over_ranks(ms, world, dev)
+        b_iter = (_side_bytes(solver.row[1], solver.row[3], solver.nr) +
+                  _side_bytes(solver.col[1], solver.col[3], solver.nc))
+        sides = {"row": "tiled" if solver.r_tiles is not None else "exact",
+                 "col": "tiled" if solver.c_tiles is not None else "exact"}
+        achieved = -max_over_ranks(-(b_iter * K / (ms / 1e3) / 1e9), world, dev)
+        solver.close()
+    value = K / (ms / 1e3)
+    if rank == 0:
+        line = _base_line("cfg5", w, value, UNIT, world, K, max(args.warmup, 3), ms / K, clocks, {
+            "nnz": nnz, "setup_ms": round(setup_ms, 1), "sides": sides,
+            "parallelism": "single GPU" if world == 1 else
+            f"rows and columns partitioned over {world} GPUs; potential slices exchanged by "
+            f"peer stores after every half-step",
+            "l2": "inputs larger than L2: %.2f GB of CSR+CSC streamed per rank per iteration"
+                  % (b_iter / 1e9)})
+        line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                            "unit": "GB/s", "frac": round(achieved / peak, 4),
+                            "peak_source": peak_kind, "traffic": None,
+                            "kernel": "per rank: both half-steps per iteration, algorithmic "
+                                      "bytes of the rank's slices over the loop time"}
+        line["cpu_baseline"] = None
+        line["e2e"] = None
+        line["gpu_launches"] = None
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def import_reference():
+    """The reference package (cai4cai/SinkSLOT's ``sinkslot``) from the unmodified
+    install in baseline/_ref, or None when it is not there."""
+    path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "sinkslot")):
+        return None
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    try:
+        import sinkslot
+        from sinkslot import sinkhorn_solvers  # noqa: F401
+    except Exception:
+        return None
+    return sinkslot
+
+
+def triton_reference_leg(X, Y, A, B, w, steps: int, ours: float):
+    """The reference's own GPU kernel on this device: its Triton segmented LSE
+    (sinkslot/sinkhorn_solvers.py:45-94) driven by its alternating loop
+    (:195-289) over its own CSR/CSC, built by its CUDA pipeline (the
+    "sinkslotcuda" method of its benchmark harness: CUDA builder, Triton cost,
+    narrow keys).  `steps` iterations timed with CUDA events after warm-up.
+    None when the reference package is not importable or Triton fails."""
+    ref = import_reference()
+    if ref is None:
+        return None
+    try:
+        from sinkslot import sinkhorn_solvers as rss
+        from sinkslot import solver as rs
+        n, m = w["n"], w["m"]
+        dev = X.device
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        rows, cols, S = rs.sot_plan_coo(X, Y, A, B, L=w["L"], seed=w["proj_seed"],
+                                        ot1d=rs._ot_1d_coo_batched_cuda)
+        cost = rs.sparse_sqeuclidean_cost(X, Y, rows, cols, use_triton=True)
+        lam = S.clamp_min(torch.finfo(S.dtype).tiny).log() - cost / w["eps"]
+        R = rs.to_csr(rows, cols, lam, n, narrow_key=True)
+        C = rs.to_csr(cols, rows, lam, m, narrow_key=True)
+        torch.cuda.synchronize(dev)
+        setup_ms = (time.perf_counter() - t0) * 1e3
+        nnz = int(rows.numel())
+        del rows, cols, S, cost, lam
+        la, lb = A.log(), B.log()
+        args = (R[0], R[1], R[2], C[0], C[1], C[2], la, lb, n, m)
+        rss.sinkslot_alternating_triton(*args, 5)  # JIT compile + warm-up
+        stream = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        rss.sinkslot_alternating_triton(*args, steps)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        v = steps / (ms / 1e3)
+        b_iter = nnz * (R[1].element_size() + 4) + nnz * (C[1].element_size() + 4) + 16 * (n + m)
+        return {"value": round(v, 2), "unit": UNIT, "steps": steps,
+                "gbs": round(b_iter * v / 1e9, 1), "nnz": nnz, "setup_ms": round(setup_ms, 1),
+                "speedup_of_this_build": round(ours / v, 3) if v > 0 else None,
+                "kind": "the reference's Triton kernel _seg_lse_online_kernel in its "
+                        "sinkslot_alternating_triton loop, on this B200, over its own "
+                        "CSR/CSC (unmodified install in baseline/_ref)"}
+    except Exception as exc:  # the comparison is reported, never required
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+
+
 def cpu_baseline_from_support(rows, cols, lam, log_a, log_b, w, budget_s: float = 15.0):
     """The oracle's torch-backend iteration (C, OpenMP, all host threads) on the
     same support, a bounded number of iterations."""
@@ -541,7 +1001,12 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
+                    help="workload: cfg2 the headline (default); cfg3 colour-transfer shape; "
+                         "cfg4 gradient flow; cfg5 N=M=2^24 (strong scaling under torchrun)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="skip timing the reference's Triton kernel on the same device")
     ap.add_argument("--plain", action="store_true",
                     help="time the exact half-step kernel alone (no shared-memory tiles)")
     ap.add_argument("--replicas", action="store_true",
@@ -559,6 +1024,12 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "cfg3":
+        run_cfg3(args)
+    elif args.config == "cfg4":
+        run_cfg4(args)
+    elif args.config == "cfg5":
+        run_cfg5(args)
     else:
         run_b200(args)
 

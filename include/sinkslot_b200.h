@@ -160,9 +160,10 @@ int sinkslot_build_tiles(const int32_t* indptr, const void* idx, int idx_bytes, 
  * their torch twins (:443-588).  stop_mode: 0 fixed (n_iters), 1 potential,
  * 2 marginal (up to max_iter, checked every check_every).  r_tiles / c_tiles
  * (each nullable) are layouts from sinkslot_build_tiles of the two sides; a
- * side with one runs the shared-memory-staged half-step in every iteration
- * after the first, a side without the exact kernel.  phi (n), psi (m) receive
- * the absorbed potentials.
+ * side with one runs the shared-memory-staged half-step (in the first
+ * iteration only the alternating variant's column half-step does, after a
+ * tiled max pass that gives its stabilisers), a side without the exact
+ * kernel.  phi (n), psi (m) receive the absorbed potentials.
  * *converged_host: -1 (fixed mode), 0 or 1; *final_viol_host: NaN in fixed
  * mode. */
 int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
@@ -182,10 +183,13 @@ int sinkslot_solve_csr(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
 /* sinkslot_solve_csr without the work buffer: the loop's scratch is the
  * library's static device array (no counterpart in the reference; for callers
  * that cannot allocate device scratch).  Allocates nothing.  Status 1 when
- * sinkslot_solve_work_floats(n, m) > SINKSLOT_STATIC_SOLVE_FLOATS.  The first
- * call on a device resolves the array's address and should come before any
- * stream capture there; calls that overlap on one device share the array and
- * race. */
+ * sinkslot_solve_work_floats(n, m) > SINKSLOT_STATIC_SOLVE_FLOATS, i.e. when
+ * 3 * (pad4(n) + pad4(m)) + 64 > 2^20 with pad4(v) = v rounded up to a multiple
+ * of 4.  The first call on a device resolves the array's address and should
+ * come before any stream capture there; the address is kept for the life of
+ * the device's primary context (a host that resets the device with
+ * cudaDeviceReset must not call this entry point on it again in the same
+ * process).  Calls that overlap on one device share the array and race. */
 int sinkslot_solve_csr_static(const int32_t* r_ptr, const void* r_idx, int r_idx_bytes,
                               const float* r_lam, const int32_t* c_ptr, const void* c_idx,
                               int c_idx_bytes, const float* c_lam, int64_t nnz,

@@ -24,6 +24,7 @@ from .gradient import (
     sparse_barycentric_map,
 )
 from .samples_loss import SamplesLoss
+from .batched import sinkslot_solve_batched
 from ._lib import LIB_PATH, SinkslotError, lib as load_library
 
 __all__ = [
@@ -39,6 +40,7 @@ __all__ = [
     "slot_grad",
     "sparse_barycentric_map",
     "SamplesLoss",
+    "sinkslot_solve_batched",
     "SinkslotError",
     "LIB_PATH",
     "load_library",

@@ -10,7 +10,9 @@
 
 namespace sinkslot {
 
-enum OutMode { kOutPlain = 0, kOutBlend = 1, kOutNone = 2 };
+// kOutMax: the tiled pass writes each segment's largest term lam + other instead
+// of a potential (the stabilisers of a following pass; tiled.cu only).
+enum OutMode { kOutPlain = 0, kOutBlend = 1, kOutNone = 2, kOutMax = 3 };
 enum CheckMode { kChkNone = 0, kChkMarg = 1, kChkPot = 2 };
 
 // Copies of a half-step's output in other GPUs' potential buffers (mapped into

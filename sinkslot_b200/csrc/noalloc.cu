@@ -12,12 +12,17 @@
 // Rules of use:
 //   - The first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current) and keeps it; make that
-//     first call before any stream capture on the device.
+//     first call before any stream capture on the device.  The kept address
+//     belongs to the device's primary context: after cudaDeviceReset (or any
+//     teardown of that context) it is stale, so a host that resets a device
+//     must not call this entry point on it again in the same process.
 //   - There is one array per device: calls that overlap on the same device
 //     (two host threads, or two streams whose work interleaves) share it and
 //     race.  Serialise them.
-//   - Problems whose scratch (sinkslot_solve_work_floats) exceeds the array
-//     are rejected with status 1; use sinkslot_solve_csr with a caller buffer.
+//   - Problems whose scratch (sinkslot_solve_work_floats: 3 * (pad4(n) +
+//     pad4(m)) + 64 floats, pad4 rounding up to a multiple of 4) exceeds the
+//     array are rejected with status 1; use sinkslot_solve_csr with a caller
+//     buffer.
 //   - Each call zeroes the part of the array it uses, on its stream, before
 //     the solve reads it.
 #include <mutex>

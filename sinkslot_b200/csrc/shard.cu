@@ -113,7 +113,7 @@ struct ShardSpec {
 static int64_t pad4s(int64_t v) { return (v + 3) & ~int64_t(3); }
 
 size_t shard_work_floats(int64_t nr, int64_t nc) {
-  return (size_t)(2 * (pad4s(nr) + pad4s(nc)) + 64);
+  return (size_t)(2 * (pad4s(nr) + pad4s(nc)) + 64 + pad4s(nc));
 }
 
 static int read_words(const void* d, void* h, size_t bytes, cudaStream_t st) {
@@ -144,7 +144,8 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
                          (sp.variant == 0 || (sp.phi[g][1] && sp.psi[g][1])),
                      "solve_shard: missing peer buffer");
   // work: prev_phi (nr) | prev_psi (nc) | 64 words: [0,1] check maxima, [2,3]
-  //       handed-back counts, [4] error, [8] publish counter | lists (nr, nc)
+  //       handed-back counts, [4] error, [8] publish counter | lists (nr, nc) |
+  //       stabilisers of the first column half-step (nc)
   const int64_t nr4 = pad4s(nr), nc4 = pad4s(nc);
   float* prev_phi = work;
   float* prev_psi = work + nr4;
@@ -154,6 +155,7 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
   unsigned int* done = acc + 8;
   int* fb_rows = reinterpret_cast<int*>(work + nr4 + nc4 + 64);
   int* fb_cols = fb_rows + nr4;
+  float* sigma0 = work + 2 * (nr4 + nc4) + 64;
   if (it0 == 0) {
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(acc, 0, 64 * sizeof(uint32_t), st));
     SINKSLOT_CUDA_TRY(cudaMemsetAsync(prev_phi, 0, (nr4 + nc4) * sizeof(float), st));
@@ -199,8 +201,14 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
       for (int g = 0; g < sp.world; ++g)
         if (g != me) po.p[po.n++] = (row ? sp.phi[g][nb] : sp.psi[g][nb]) + off;
     unsigned int ctas = 0;
+    // The first iteration (as in the single-GPU loop): a half-step that gathers
+    // the zero start potential runs the exact kernel without the gather; the
+    // alternating first column half-step with a tiled layout takes its
+    // stabilisers from a tiled max pass.
+    const bool first = it == 0 && out_mode != kOutNone;
+    const bool zero_other = first && (row || sp.variant == 1);
     if (side.nseg > 0) {
-      if (tiles != nullptr && it > 0) {
+      if (tiles != nullptr && (it > 0 || (first && !zero_other))) {
         TiledHalfStep t;
         t.g = row ? sp.row_geom : sp.col_geom;
         t.layout = tiles;
@@ -221,15 +229,19 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
         t.fb_count_reset = fb_count + (row ? 1 : 0);
         // This side's counter is zeroed by the other side's tiled launch; when the
         // other side runs exact, zero it here.
-        if ((row ? sp.col_tiles : sp.row_tiles) == nullptr)
+        if ((row ? sp.col_tiles : sp.row_tiles) == nullptr || it == 0)
           SINKSLOT_CUDA_TRY(cudaMemsetAsync(t.fb_count, 0, sizeof(int), st));
         t.err = perr;
         t.peers = po;
         t.done = done;
+        if (it == 0) {
+          t.sigma = sigma0;
+          SINKSLOT_TRY(tiled_max_pass(t, sigma0, st));
+        }
         SINKSLOT_TRY(tiled_half_step(t, out_mode, chk, st, &ctas));
       } else {
         HalfStep h = side;
-        h.other = other;
+        h.other = zero_other ? nullptr : other;
         h.base = base;
         h.prev = prev;
         h.acc = acc_side;

@@ -30,7 +30,10 @@ constexpr int kLseUnroll = 4;
 
 // One half-step over the segments of a CSR side, by the whole grid: G lanes
 // per segment, online max / sum, then the epilogue; the check maxima go to acc.
-template <typename IT, int G, int OUT, int CHK>
+// ZO: the gathered potential is identically zero (`other` is null): the terms
+// are lam + p + 0, the same bits as gathering a zero-filled vector, and the
+// index stream is not read at all (the first half-step of every solve).
+template <typename IT, int G, int OUT, int CHK, bool ZO>
 __device__ __forceinline__ void seg_pass(const int32_t* __restrict__ ptr,
                                          const IT* __restrict__ idx,
                                          const float* __restrict__ lam,
@@ -70,12 +73,14 @@ __device__ __forceinline__ void seg_pass(const int32_t* __restrict__ ptr,
 #pragma unroll
       for (int u = 0; u < kLseUnroll; ++u) {
         kk[u] = k0 + u * G + lane;
-        ci[u] = kk[u] < end ? ld_stream(idx + kk[u]) : IT(0);
+        ci[u] = (!ZO && kk[u] < end) ? ld_stream(idx + kk[u]) : IT(0);
         lv[u] = kk[u] < end ? ld_stream(lam + kk[u]) : 0.0f;
       }
 #pragma unroll
       for (int u = 0; u < kLseUnroll; ++u)
-        v[u] = kk[u] < end ? __fadd_rn(__fadd_rn(lv[u], p), __ldg(other + (int64_t)ci[u])) : -INFINITY;
+        v[u] = kk[u] < end ? __fadd_rn(__fadd_rn(lv[u], p),
+                                       ZO ? 0.0f : __ldg(other + (int64_t)ci[u]))
+                           : -INFINITY;
       float bm = v[0];
 #pragma unroll
       for (int u = 1; u < kLseUnroll; ++u) bm = fmaxf(bm, v[u]);
@@ -117,8 +122,12 @@ __global__ void __launch_bounds__(kLseThreads) half_step_kernel(
     uint32_t* acc, const int* __restrict__ list, const int* __restrict__ list_count,
     const PeerOut po, unsigned int* done) {
   chain_enter();
-  seg_pass<IT, G, OUT, CHK>(ptr, idx, lam, other, selfpot, base, self_old, out, nseg, w_old,
-                            w_new, prev, acc, list, list_count, po);
+  if (other != nullptr)
+    seg_pass<IT, G, OUT, CHK, false>(ptr, idx, lam, other, selfpot, base, self_old, out, nseg,
+                                     w_old, w_new, prev, acc, list, list_count, po);
+  else
+    seg_pass<IT, G, OUT, CHK, true>(ptr, idx, lam, other, selfpot, base, self_old, out, nseg,
+                                    w_old, w_new, prev, acc, list, list_count, po);
   chain_release();
   if (po.n > 0) {
     __syncthreads();
@@ -257,11 +266,18 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
   float* psi_nx = psi_next;
   int64_t it = 0;
 
-  // One half-step of either side.  The first iteration runs the exact kernel
-  // (the starting potentials are no estimate of the LSE the tiled pass needs as
-  // its stabiliser); later ones the tiled pass plus the exact pass over the rows
-  // it hands back.
-  auto side_step = [&](bool row, int out_mode, int chk) -> int {
+  // One half-step of either side.  Later iterations run the tiled pass (where a
+  // side has a tiled layout) plus the exact pass over the rows it hands back,
+  // stabilised by each row's previous log-sum-exp.  The first iteration has no
+  // previous log-sum-exp:
+  //   * a half-step that gathers the zero start potential (the row side, and
+  //     both sides of the symmetric variant) runs the exact kernel without
+  //     gathering (its terms are lam itself);
+  //   * the alternating variant's first column half-step gathers the fresh
+  //     row potential: with a tiled layout, a tiled max pass writes each
+  //     column's largest term, and the tiled pass uses those as stabilisers
+  //     (every term <= 1, every sum >= 1); without one, the exact kernel.
+  auto side_step = [&](bool row, int out_mode, int chk, bool first) -> int {
     const HalfStep& side = row ? sp.row : sp.col;
     float* self_cur = row ? phi_cur : psi_cur;
     float* self_nx = row ? phi_nx : psi_nx;
@@ -271,7 +287,8 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
     uint32_t* acc_side = acc + (row ? 0 : 1);
     float* out = sp.variant == 0 ? self_cur : self_nx;  // Gauss-Seidel: in place
     const void* tiles = row ? sp.row_tiles : sp.col_tiles;
-    if (tiles != nullptr && it > 0) {
+    const bool zero_other = first && (row || sp.variant == 1);
+    if (tiles != nullptr && (it > 0 || (first && !zero_other))) {
       TiledHalfStep t;
       t.g = row ? sp.row_geom : sp.col_geom;
       t.layout = tiles;
@@ -292,13 +309,19 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
       t.fb_count_reset = fb_count + (row ? 1 : 0);
       // This side's counter is zeroed by the other side's tiled launch; when the
       // other side runs exact, zero it here.
-      if ((row ? sp.col_tiles : sp.row_tiles) == nullptr)
+      if ((row ? sp.col_tiles : sp.row_tiles) == nullptr || it == 0)
         SINKSLOT_CUDA_TRY(cudaMemsetAsync(t.fb_count, 0, sizeof(int), st));
       t.err = perr;
+      if (it == 0) {
+        // the alternating variant's first column half-step: psi_next is unused
+        // by that variant and holds the stabilisers
+        t.sigma = self_nx;
+        SINKSLOT_TRY(tiled_max_pass(t, self_nx, st));
+      }
       return tiled_half_step(t, out_mode, chk, st);
     }
     HalfStep h = side;
-    h.other = other;
+    h.other = zero_other ? nullptr : other;
     h.base = base;
     h.prev = prev;
     h.acc = acc_side;
@@ -308,8 +331,14 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
     h.out = out;
     return half_step(h, out_mode, chk, st);
   };
-  auto row_step = [&](int out_mode, int chk) { return side_step(true, out_mode, chk); };
-  auto col_step = [&](int out_mode, int chk) { return side_step(false, out_mode, chk); };
+  // `first`: the iteration's own half-step (false for the symmetric variant's
+  // check-only half-steps, which read the blended state)
+  auto row_step = [&](int out_mode, int chk, bool first = true) {
+    return side_step(true, out_mode, chk, first && it == 0);
+  };
+  auto col_step = [&](int out_mode, int chk, bool first = true) {
+    return side_step(false, out_mode, chk, first && it == 0);
+  };
   auto swap_sym = [&]() {
     float* t = phi_cur; phi_cur = phi_nx; phi_nx = t;
     t = psi_cur; psi_cur = psi_nx; psi_nx = t;
@@ -361,8 +390,8 @@ int solve_loop(const SolveSpec& sp, float* phi, float* psi, float* work, int64_t
         SINKSLOT_TRY(col_step(kOutBlend, kChkNone));
         swap_sym();
         if (chk) {
-          SINKSLOT_TRY(row_step(kOutNone, kChkMarg));
-          SINKSLOT_TRY(col_step(kOutNone, kChkMarg));
+          SINKSLOT_TRY(row_step(kOutNone, kChkMarg, false));
+          SINKSLOT_TRY(col_step(kOutNone, kChkMarg, false));
         }
       }
       ++it;

@@ -455,9 +455,14 @@ __global__ void run_sum_kernel(const uint64_t* __restrict__ key, const uint32_t*
   }
 }
 
-__global__ void export_kernel(const uint64_t* __restrict__ ukey, const float* __restrict__ Sin,
+__device__ __forceinline__ const float* support_s(const uint32_t* rm, const uint32_t* rm2,
+                                                   const int64_t* scal);
+
+__global__ void export_kernel(const uint64_t* __restrict__ ukey, const uint32_t* rm,
+                              const uint32_t* rm2, const int64_t* __restrict__ scal,
                               int64_t nnz, int64_t m, int64_t* __restrict__ rows,
                               int64_t* __restrict__ cols, float* __restrict__ S) {
+  const float* __restrict__ Sin = support_s(rm, rm2, scal);
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nnz;
        k += (int64_t)gridDim.x * blockDim.x) {
     const uint64_t kk = ukey[k];
@@ -571,9 +576,16 @@ struct SupportBufs {
   uint32_t *rm, *rm2;
   int64_t *chist, *cstmp;
   uint64_t* ukey;
-  float* S;
-  int64_t* scal;  // [0] raw total of a batch, [1] unique count
+  // the unique entries' S sits in whichever of rm / rm2 the sort left free
+  // (scal[2] = 1: rm2 holds the sorted masses, S is in rm)
+  int64_t* scal;  // [0] raw total of a batch, [1] unique count, [2] S buffer selector
 };
+
+// the S of the unique entries (see SupportBufs)
+__device__ __forceinline__ const float* support_s(const uint32_t* rm, const uint32_t* rm2,
+                                                   const int64_t* scal) {
+  return reinterpret_cast<const float*>(scal[2] ? rm : rm2);
+}
 
 static int chunk_of(int L, int chunk) { return (chunk <= 0 || chunk > L) ? L : chunk; }
 
@@ -587,7 +599,6 @@ static void carve_support(Carver& cv, SupportBufs& b, int64_t n, int64_t m, int 
   b.chist = cv.take<int64_t>(std::max<int64_t>(nh, 1));
   b.cstmp = cv.take<int64_t>(scan_tmp_elems(std::max<int64_t>(nh, cap)));
   b.ukey = cv.take<uint64_t>(cap);
-  b.S = cv.take<float>(cap);
   b.scal = cv.take<int64_t>(8);
 }
 
@@ -648,8 +659,11 @@ int build_support(const float* X, const float* Y, const float* a, const float* b
   SINKSLOT_CHECK_LAUNCH();
   SINKSLOT_TRY(scan_exclusive_i64(uidx, nraw, b.cstmp, b.scal + 1, stream));
   const float invL = 1.0f / (float)L;
-  run_sum_kernel<<<grid_for(nraw, 256), 256, 0, stream>>>(skey, smass, nraw, uidx, invL, b.ukey,
-                                                         b.S);
+  // S of the unique entries goes into the mass buffer the sort left free
+  float* S = reinterpret_cast<float*>(alt ? b.rm : b.rm2);
+  const int64_t sel = alt ? 1 : 0;  // pageable source: staged before the call returns
+  SINKSLOT_CUDA_TRY(cudaMemcpyAsync(b.scal + 2, &sel, sizeof(sel), cudaMemcpyHostToDevice, stream));
+  run_sum_kernel<<<grid_for(nraw, 256), 256, 0, stream>>>(skey, smass, nraw, uidx, invL, b.ukey, S);
   SINKSLOT_CHECK_LAUNCH();
   return read_i64(b.scal + 1, nnz_out, stream);
 }
@@ -666,7 +680,8 @@ int support_export(const void* ws, size_t ws_bytes, int64_t n, int64_t m, int d,
   }
   SINKSLOT_REQUIRE(nnz >= 0 && nnz <= (int64_t)L * (n + m), "support_export: bad nnz");
   if (nnz == 0) return kOk;
-  export_kernel<<<grid_for(nnz, 256), 256, 0, stream>>>(b.ukey, b.S, nnz, m, rows, cols, S);
+  export_kernel<<<grid_for(nnz, 256), 256, 0, stream>>>(b.ukey, b.rm, b.rm2, b.scal, nnz, m, rows,
+                                                        cols, S);
   SINKSLOT_CHECK_LAUNCH();
   return kOk;
 }

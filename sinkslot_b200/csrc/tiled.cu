@@ -915,6 +915,7 @@ struct TKArgs {
   const float* other;
   const float* base;
   const float* self_old;
+  const float* sigma;  // optional stabilisers (else base - self_old)
   float* out;
   float w_old, w_new;
   float* prev;
@@ -1027,6 +1028,25 @@ __device__ __forceinline__ void process_group(unsigned char* smem, uint32_t* fla
   }
 }
 
+// Max mode: the largest term lam + cur[column] of each row, as the
+// order-preserving integer image of the float (float_to_radix) in the row's
+// first sum word, which starts at 0 (below the image of every float).
+// Padding adds -inf to the dummy row.
+__device__ __forceinline__ void process_group_max(unsigned char* smem, const float* cur,
+                                                  const uint2 (&e)[kGroup], int cnt) {
+#pragma unroll
+  for (int j = 0; j < kGroup; ++j) {
+    if (j < cnt) {
+      uint32_t* st = row_state(smem, e[j].x >> 16);
+      atomicMax(st + 1, float_to_radix(__fadd_rn(__uint_as_float(e[j].y), cur[e[j].x & 0xFFFFu])));
+    }
+  }
+}
+
+__device__ __forceinline__ float radix_to_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
 template <int OUT, int CHK>
 __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const TKArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -1135,8 +1155,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       if (r <= a.R) {
         uint32_t* st = row_state(smem, (uint32_t)r);
         float sg = 0.0f;
-        if (r < rows) {
-          sg = __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
+        if (r < rows && OUT != kOutMax) {
+          sg = a.sigma ? a.sigma[row0 + r] : __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
           longrow = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
         }
         st[0] = __float_as_uint(sg);
@@ -1179,7 +1199,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
           load_group(a.ent, e0, nsl, g + kStep, lane, en);
         else
           load_group(a.ent, f0, nsl_next, kGroup * warp, lane, en);
-        process_group(smem, flags, cur, e, nsl - g, capd);
+        if (OUT == kOutMax)
+          process_group_max(smem, cur, e, nsl - g);
+        else
+          process_group(smem, flags, cur, e, nsl - g, capd);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(pot_empty(s));
@@ -1191,6 +1214,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     for (int r = tid; r < rows; r += kConsumers) {
       const int64_t seg = row0 + r;
       const uint32_t* st = row_state(smem, (uint32_t)r);
+      if (OUT == kOutMax) {
+        a.out[seg] = st[1] ? radix_to_float(st[1]) : -INFINITY;
+        continue;
+      }
       const unsigned long long q = ((unsigned long long)st[1] << kLoBits) + st[2];
       const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
       if (flagged || q < kFixMin) {
@@ -1231,14 +1258,7 @@ static int launch_tiled(const TKArgs& a, size_t smem, cudaStream_t st) {
   return kOk;
 }
 
-int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st,
-                    unsigned int* ctas) {
-  SINKSLOT_REQUIRE(h.base != nullptr, "tiled half step: base is required");
-  SINKSLOT_REQUIRE(h.fb_count && h.fb_list && h.err, "tiled half step: fallback list is required");
-  SINKSLOT_REQUIRE(out_mode != kOutNone || chk == kChkMarg, "half step: check-only needs a check");
-  SINKSLOT_REQUIRE((reinterpret_cast<uintptr_t>(h.other) & 15u) == 0,
-                   "tiled half step: the gathered potential must be 16-byte aligned");
-  if (h.g.nseg <= 0) return kOk;
+static TKArgs tk_args(const TiledHalfStep& h) {
   LayoutPtrs L = carve_layout(const_cast<void*>(h.layout), h.g);
   TKArgs a;
   a.nseg = h.g.nseg;
@@ -1254,6 +1274,7 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.other = h.other;
   a.base = h.base;
   a.self_old = h.self_old;
+  a.sigma = h.sigma;
   a.out = h.out;
   a.w_old = h.w_old;
   a.w_new = h.w_new;
@@ -1265,19 +1286,13 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   a.err = h.err;
   a.peers = h.peers;
   a.done = h.done;
-  const size_t smem = h.g.smem_bytes;
-  if (out_mode == kOutPlain) {
-    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkNone>(a, smem, st)));
-    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkMarg>(a, smem, st)));
-    else SINKSLOT_TRY((launch_tiled<kOutPlain, kChkPot>(a, smem, st)));
-  } else if (out_mode == kOutBlend) {
-    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutBlend, kChkNone>(a, smem, st)));
-    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled<kOutBlend, kChkMarg>(a, smem, st)));
-    else SINKSLOT_TRY((launch_tiled<kOutBlend, kChkPot>(a, smem, st)));
-  } else {
-    SINKSLOT_TRY((launch_tiled<kOutNone, kChkMarg>(a, smem, st)));
-  }
-  // exact pass over the rows the tiled pass handed back
+  return a;
+}
+
+static int exact_handed_back(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st,
+                             unsigned int* ctas) {
+  // exact pass over the rows the tiled pass handed back (stabilised by their
+  // own running maximum: the exact kernel needs no sigma)
   HalfStep x;
   x.ptr = h.ptr;
   x.idx = h.idx;
@@ -1300,5 +1315,44 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
   if (ctas) *ctas += (unsigned)std::min(h.g.P, num_sms());
   return half_step(x, out_mode, chk, st, ctas);
 }
+
+int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st,
+                    unsigned int* ctas) {
+  SINKSLOT_REQUIRE(h.base != nullptr, "tiled half step: base is required");
+  SINKSLOT_REQUIRE(h.fb_count && h.fb_list && h.err, "tiled half step: fallback list is required");
+  SINKSLOT_REQUIRE(out_mode != kOutNone || chk == kChkMarg, "half step: check-only needs a check");
+  SINKSLOT_REQUIRE((reinterpret_cast<uintptr_t>(h.other) & 15u) == 0,
+                   "tiled half step: the gathered potential must be 16-byte aligned");
+  if (h.g.nseg <= 0) return kOk;
+  const TKArgs a = tk_args(h);
+  const size_t smem = h.g.smem_bytes;
+  if (out_mode == kOutPlain) {
+    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkNone>(a, smem, st)));
+    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkMarg>(a, smem, st)));
+    else SINKSLOT_TRY((launch_tiled<kOutPlain, kChkPot>(a, smem, st)));
+  } else if (out_mode == kOutBlend) {
+    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutBlend, kChkNone>(a, smem, st)));
+    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled<kOutBlend, kChkMarg>(a, smem, st)));
+    else SINKSLOT_TRY((launch_tiled<kOutBlend, kChkPot>(a, smem, st)));
+  } else {
+    SINKSLOT_TRY((launch_tiled<kOutNone, kChkMarg>(a, smem, st)));
+  }
+  return exact_handed_back(h, out_mode, chk, st, ctas);
+}
+
+int tiled_max_pass(const TiledHalfStep& h, float* sigma_out, cudaStream_t st, unsigned int* ctas) {
+  SINKSLOT_REQUIRE(sigma_out != nullptr && h.err, "tiled max pass: bad arguments");
+  SINKSLOT_REQUIRE((reinterpret_cast<uintptr_t>(h.other) & 15u) == 0,
+                   "tiled half step: the gathered potential must be 16-byte aligned");
+  if (h.g.nseg <= 0) return kOk;
+  TKArgs a = tk_args(h);
+  a.out = sigma_out;
+  a.peers.n = 0;
+  a.fb_reset = nullptr;
+  SINKSLOT_TRY((launch_tiled<kOutMax, kChkNone>(a, h.g.smem_bytes, st)));
+  if (ctas) *ctas += (unsigned)std::min(h.g.P, num_sms());
+  return kOk;
+}
+
 
 }  // namespace sinkslot

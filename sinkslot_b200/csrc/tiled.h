@@ -43,6 +43,9 @@ struct TiledHalfStep {
   const float* other = nullptr;
   const float* base = nullptr;
   const float* self_old = nullptr;
+  // optional per-segment stabilisers; without them a segment's stabiliser is
+  // base - self_old, the log-sum-exp of its previous half-step
+  const float* sigma = nullptr;
   float* out = nullptr;
   float w_old = 0.5f, w_new = 0.5f;
   float* prev = nullptr;
@@ -59,5 +62,13 @@ struct TiledHalfStep {
 // increased by the number of CTAs launched
 int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t st,
                     unsigned int* ctas = nullptr);
+
+// One tiled pass that writes, for every segment s, max_k (lam_k + other[idx_k])
+// into sigma_out[s] (-inf for an empty segment; NaN when a term is NaN).  Used
+// as the stabilisers of a tiled half-step that has no previous log-sum-exp (the
+// first column half-step of a solve): every term of that pass is then at most
+// 1 and every sum at least 1, so no segment is handed back for its range.
+int tiled_max_pass(const TiledHalfStep& h, float* sigma_out, cudaStream_t st,
+                   unsigned int* ctas = nullptr);
 
 }  // namespace sinkslot

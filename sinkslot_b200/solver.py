@@ -9,7 +9,7 @@ Parity notes (the support is integer work and is bit-exact against the
 reference's CUDA builder, ``_ot_1d_coo_batched_cuda``):
 
 * projections are the sequential fp32 FMA chain over ``d`` (cuBLAS's result
-  for K = d);
+  for these K = d; for d > 4 cuBLAS's own product is used);
 * the per-slice argsort is stable with -0.0 == +0.0 (CUB radix sort);
 * ``cumsum(a[ix])`` follows torch's CUDA innermost-dim scan association order;
 * duplicate entries are summed in emission order and scaled by ``1/L`` (torch's
@@ -116,6 +116,10 @@ def _ot_1d_coo_batched_cuda(PX: torch.Tensor, PY: torch.Tensor, a: torch.Tensor,
 ot_1d_coo_batched = _ot_1d_coo_batched_cuda
 
 
+# widest d for which the support builder projects with its own kernel
+OWN_PROJECTION_MAX_D = 4
+
+
 @jaxtyped(typechecker=beartype)
 def sot_plan_coo(
     X: Float[torch.Tensor, "n d"], Y: Float[torch.Tensor, "m d"],
@@ -140,16 +144,22 @@ def sot_plan_coo(
     ck = 0 if chunk is None else int(chunk)
     if chunk is not None and ck < 1:
         raise ValueError("chunk must be a positive int")
-    # Projections by the same GEMM the reference issues, chunk by chunk
-    # (solver.py:219-221): cuBLAS picks its kernel from the shape, and its
-    # rounding is the reference's definition of the sort keys.
-    step = L if chunk is None else ck
-    if step >= L:
-        PX, PY = X @ thetas.T, Y @ thetas.T
-    else:
-        PX = torch.cat([X @ thetas[s:s + step].T for s in range(0, L, step)], dim=1)
-        PY = torch.cat([Y @ thetas[s:s + step].T for s in range(0, L, step)], dim=1)
-    PX, PY = PX.contiguous(), PY.contiguous()
+    # The sort keys are the reference's projections `X @ theta.T`, chunk by
+    # chunk (solver.py:219-221).  For d <= OWN_PROJECTION_MAX_D the library
+    # computes them itself, fused into the key generation, as the sequential
+    # fp32 FMA chain over d -- bit-equal to cuBLAS's product at these d for every
+    # workload shape (tested on the device) -- so no (n, L) projection matrix is
+    # materialised.  Wider d: cuBLAS's rounding there can differ from the
+    # chain, so the product is taken from cuBLAS itself.
+    PX = PY = None
+    if d > OWN_PROJECTION_MAX_D:
+        step = L if chunk is None else ck
+        if step >= L:
+            PX, PY = X @ thetas.T, Y @ thetas.T
+        else:
+            PX = torch.cat([X @ thetas[s:s + step].T for s in range(0, L, step)], dim=1)
+            PY = torch.cat([Y @ thetas[s:s + step].T for s in range(0, L, step)], dim=1)
+        PX, PY = PX.contiguous(), PY.contiguous()
     nb = _lib.out_i64()
     call("sinkslot_support_workspace_bytes", n, m, d, L, ck, ctypes.byref(nb))
     ws = _ws(nb.value, dev)

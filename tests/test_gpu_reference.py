@@ -1,0 +1,314 @@
+"""Parity against the reference package itself, run on the same B200.
+
+The reference (cai4cai/SinkSLOT's ``sinkslot``, the unmodified install in
+``baseline/_ref``) runs on the same device and inputs with both of its
+backends: ``backend="torch"`` (its torch-op loop on CUDA tensors, the parity
+reference) and ``backend="triton"`` (its Triton kernel).
+
+Bars:
+
+* support: rows, cols and S bit-identical to the reference's CUDA run;
+* cost: bit-identical to the reference's torch cost expression on the device;
+* potentials: rtol 1e-4 / atol 1e-5 against the torch backend, after removing
+  the common (+c, -c) shift Sinkhorn leaves undamped.  At eps = 0.01 the
+  potentials reach |phi| ~ 2e3 (float32 spacing 1e-4 there), and after
+  hundreds of iterations the reference's own Triton backend disagrees with its
+  torch backend on a few hundred near-zero potentials by up to ~1e-2: that is
+  the float32 noise floor of the problem.  So the bar is: every potential within
+  rtol/atol except at most 2x as many as the reference's Triton-vs-torch
+  disagreement (+16), no deviation larger than 2x the largest of that
+  disagreement, and accuracy against the float64 iteration on the same inputs
+  no worse than 1.5x the torch backend's own;
+* stop modes: the same convergence flag, iteration counts within one check
+  interval.
+
+Skipped when the reference package is not installed in baseline/_ref.
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+RTOL, ATOL = 1e-4, 1e-5
+
+
+def _reference():
+    if not os.path.isdir(os.path.join(REF, "sinkslot")):
+        pytest.skip("the reference package is not installed in baseline/_ref")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import sinkslot
+    return sinkslot
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    torch.backends.cuda.matmul.allow_tf32 = False
+    import sinkslot_b200
+    sinkslot_b200.load_library()
+    return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return _reference()
+
+
+def _gauge(p, q, p_ref, q_ref):
+    """Median of the common shift (phi + c, psi - c) between two solutions."""
+    d = torch.cat([(p.double() - p_ref.double()), -(q.double() - q_ref.double())])
+    d = d[torch.isfinite(d)]
+    return float(d.median()) if d.numel() else 0.0
+
+
+def _disagreement(p, q, p_ref, q_ref):
+    """(count outside rtol/atol, largest deviation) after removing the shift."""
+    c = _gauge(p, q, p_ref, q_ref)
+    count, worst = 0, 0.0
+    for u, v, s in ((p, p_ref, c), (q, q_ref, -c)):
+        fin = torch.isfinite(v)
+        assert torch.equal(torch.isfinite(u), fin), "non-finite pattern differs"
+        d = (u.double() - v.double() - s)[fin].abs()
+        count += int((d > ATOL + RTOL * v.double()[fin].abs()).sum())
+        worst = max(worst, float(d.max()) if d.numel() else 0.0)
+    return count, worst
+
+
+def _assert_within_noise_floor(ours, triton, torch_ref, name):
+    n_ours, w_ours = _disagreement(ours[0], ours[1], torch_ref[0], torch_ref[1])
+    n_tri, w_tri = _disagreement(triton[0], triton[1], torch_ref[0], torch_ref[1])
+    assert n_ours <= 2 * n_tri + 16, \
+        f"{name}: {n_ours} potentials outside rtol/atol (reference Triton vs torch: {n_tri})"
+    assert w_ours <= 2 * w_tri + ATOL, \
+        f"{name}: max deviation {w_ours:.3e} (reference Triton vs torch: {w_tri:.3e})"
+    return n_ours, n_tri
+
+
+def _gauss(n, m, d, seed, shift, weights="uniform"):
+    torch.manual_seed(seed)
+    x = torch.randn(n, d)
+    y = torch.randn(m, d) + shift
+    if weights == "uniform":
+        return x, y, None, None
+    a = -torch.rand(n).clamp_min(1e-12).log()
+    b = -torch.rand(m).clamp_min(1e-12).log()
+    return x, y, a / a.sum(), b / b.sum()
+
+
+def test_headline_problem_matches_reference(cuda, ref):
+    """N = M = 2^20, d = 3, L = 64, eps = 0.01, 500 alternating iterations (the
+    benchmark's workload): support and S bit-identical to the reference's CUDA
+    run; potentials within the noise floor of the reference's two backends;
+    accuracy against float64 no worse than the torch backend's."""
+    from sinkslot_b200 import sinkslot_solve
+    from sinkslot import sinkhorn_solvers as rss
+    from sinkslot import solver as rs
+    x, y, _, _ = _gauss(1 << 20, 1 << 20, 3, 1, 1.5)
+    X, Y = x.to(cuda), y.to(cuda)
+    kw = dict(eps=0.01, L=64, seed=0, n_iters=500)
+    r_t = ref.sinkslot_solve(X, Y, backend="torch", **kw)
+    r_tr = ref.sinkslot_solve(X, Y, backend="triton", **kw)
+    ours = sinkslot_solve(X, Y, **kw)
+    assert torch.equal(ours.rows, r_t.rows) and torch.equal(ours.cols, r_t.cols)
+    assert torch.equal(ours.S, r_t.S)
+    _assert_within_noise_floor((ours.phi, ours.psi), (r_tr.phi, r_tr.psi), (r_t.phi, r_t.psi),
+                               "headline")
+    # float64 iteration of the reference's torch loop on the same support and lam
+    cost = rs.sparse_sqeuclidean_cost(X, Y, r_t.rows, r_t.cols, use_triton=False)
+    lam = (r_t.S.clamp_min(torch.finfo(torch.float32).tiny).log() - cost / 0.01).double()
+    la = torch.full((1 << 20,), 1.0 / (1 << 20), device=cuda, dtype=torch.float64).log()
+    phi64, psi64, *_ = rss.sinkslot_alternating_torch(r_t.rows, r_t.cols, lam, la, la, 1 << 20,
+                                                      1 << 20, 500)
+    for mine, theirs, truth in ((ours.phi, r_t.phi, phi64), (ours.psi, r_t.psi, psi64)):
+        e_mine = (mine.double() - truth).abs()
+        e_ref = (theirs.double() - truth).abs()
+        assert float(e_mine.max()) <= 1.5 * float(e_ref.max()) + ATOL
+        q = torch.tensor([0.5, 0.999], device=cuda, dtype=torch.float64)
+        qm, qr = torch.quantile(e_mine[::8], q), torch.quantile(e_ref[::8], q)
+        assert bool((qm <= 1.5 * qr + ATOL).all()), f"{qm.tolist()} vs {qr.tolist()}"
+
+
+CASES = [
+    # n, m, d, seed, shift, weights, eps, L, iters
+    (20000, 20000, 3, 5, 1.0, "uniform", 0.05, 64, 300),
+    (30000, 17000, 2, 6, 2.0, "dirichlet", 0.02, 48, 300),
+    (70000, 90000, 3, 7, 0.5, "dirichlet", 0.01, 32, 200),   # tiled path on both sides
+]
+
+
+@pytest.mark.parametrize("variant", ["alternating", "symmetric"])
+@pytest.mark.parametrize("case", CASES)
+def test_fixed_solves_match_reference(cuda, ref, case, variant):
+    from sinkslot_b200 import sinkslot_solve
+    n, m, d, seed, shift, weights, eps, L, iters = case
+    x, y, a, b = _gauss(n, m, d, seed, shift, weights)
+    t = [v.to(cuda) if v is not None else None for v in (x, y, a, b)]
+    kw = dict(eps=eps, L=L, seed=0, n_iters=iters, variant=variant)
+    r_t = ref.sinkslot_solve(*t, backend="torch", **kw)
+    r_tr = ref.sinkslot_solve(*t, backend="triton", **kw)
+    ours = sinkslot_solve(*t, **kw)
+    assert torch.equal(ours.rows, r_t.rows) and torch.equal(ours.cols, r_t.cols)
+    # duplicate masses are summed by atomics in the reference: one rounding apart
+    torch.testing.assert_close(ours.S, r_t.S, rtol=3e-7, atol=0)
+    assert ours.iters_run == r_t.iters_run == iters
+    _assert_within_noise_floor((ours.phi, ours.psi), (r_tr.phi, r_tr.psi), (r_t.phi, r_t.psi),
+                               f"{case} {variant}")
+
+
+@pytest.mark.parametrize("variant", ["alternating", "symmetric"])
+@pytest.mark.parametrize("mode,tol", [("marginal", 1e-6), ("potential", 1e-5)])
+def test_stop_modes_match_reference(cuda, ref, variant, mode, tol):
+    from sinkslot_b200 import sinkslot_solve
+    x, y, a, b = _gauss(9000, 7000, 3, 8, 1.0, "dirichlet")
+    t = [v.to(cuda) for v in (x, y, a, b)]
+    kw = dict(eps=0.05, L=40, seed=0, stop_mode=mode, stop_max_iter=20000, stop_tol=tol,
+              stop_check_every=5, variant=variant)
+    r_t = ref.sinkslot_solve(*t, backend="torch", **kw)
+    r_tr = ref.sinkslot_solve(*t, backend="triton", **kw)
+    ours = sinkslot_solve(*t, **kw)
+    assert ours.converged == r_t.converged
+    assert abs(ours.iters_run - r_t.iters_run) <= 5
+    assert abs(r_tr.iters_run - r_t.iters_run) <= 5
+    c = _gauge(ours.phi, ours.psi, r_t.phi, r_t.psi)
+    torch.testing.assert_close(ours.phi - c, r_t.phi, rtol=0, atol=5e-3)
+    torch.testing.assert_close(ours.psi + c, r_t.psi, rtol=0, atol=5e-3)
+
+
+def test_cost_and_lam_bits_match_reference(cuda, ref):
+    """The fused cost kernel against the reference's torch cost expression on the
+    device: bit-identical; lam against the reference's expression (sinkhorn_
+    solvers.py:700) on the device: within one float32 rounding of the division."""
+    from sinkslot_b200 import sparse_sqeuclidean_cost
+    from sinkslot_b200.solver import cost_and_lam
+    from sinkslot import solver as rs
+    x, y, a, b = _gauss(50000, 40000, 3, 9, 1.0, "dirichlet")
+    X, Y, A, B = (v.to(cuda) for v in (x, y, a, b))
+    rows, cols, S = rs.sot_plan_coo(X, Y, A, B, L=32, seed=0, ot1d=rs._ot_1d_coo_batched_cuda)
+    want = rs.sparse_sqeuclidean_cost(X, Y, rows, cols, use_triton=False)
+    got = sparse_sqeuclidean_cost(X, Y, rows, cols)
+    assert torch.equal(got, want)
+    lam, cost = cost_and_lam(X, Y, rows, cols, S, 0.01, want_cost=True)
+    assert torch.equal(cost, want)
+    lam_ref = S.clamp_min(torch.finfo(S.dtype).tiny).log() - want / 0.01
+    torch.testing.assert_close(lam, lam_ref, rtol=2 ** -23, atol=0)
+
+
+def test_plan_gradient_and_loss_match_reference(cuda, ref):
+    """sparse_transport_plan, sparse_barycentric_map, slot_grad and SamplesLoss
+    (value and backward) against the reference's torch backend on the device."""
+    import sinkslot_b200 as B2
+    x, y, a, b = _gauss(6000, 5000, 3, 10, 1.0, "dirichlet")
+    X, Y, A, Bw = (v.to(cuda) for v in (x, y, a, b))
+    kw = dict(eps=0.05, L=32, seed=0, n_iters=300)
+    P = B2.sparse_transport_plan(X, Y, A, Bw, **kw)
+    Pr = ref.sparse_transport_plan(X, Y, A, Bw, backend="torch", **kw)
+    assert torch.equal(P.indices(), Pr.indices())
+    torch.testing.assert_close(P.values(), Pr.values(), rtol=1e-3, atol=1e-9)
+    Tx, Ty = B2.sparse_barycentric_map(P, X, Y)
+    Txr, Tyr = ref.sparse_barycentric_map(Pr, X, Y)
+    torch.testing.assert_close(Tx, Txr, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(Ty, Tyr, rtol=1e-4, atol=1e-5)
+    g = B2.slot_grad(X, Y, A, Bw, 0.05, 32, 0, 300)
+    gr = ref.slot_grad(X, Y, A, Bw, 0.05, 32, 0, 300, backend="torch")
+    torch.testing.assert_close(g, gr, rtol=1e-4, atol=1e-5 * float(gr.abs().max()))
+    xr = X.clone().requires_grad_(True)
+    loss = B2.SamplesLoss(eps=0.05, L=32, n_iters=300)(xr, Y, A, Bw)
+    (gx,) = torch.autograd.grad(loss, [xr])
+    xr2 = X.clone().requires_grad_(True)
+    loss_r = ref.SamplesLoss(eps=0.05, L=32, n_iters=300, backend="torch")(xr2, Y, A, Bw)
+    (gx2,) = torch.autograd.grad(loss_r, [xr2])
+    assert float(loss) == pytest.approx(float(loss_r), rel=1e-4, abs=1e-6)
+    torch.testing.assert_close(gx, gx2, rtol=1e-4, atol=1e-5 * float(gx2.abs().max()))
+
+
+def test_reference_dispatch_reaches_this_backend(cuda, ref, tmp_path):
+    """The reference-side dispatch patch (the maintainer's edit of
+    sinkhorn_solvers.py, tests/reference_dispatch_patch.py) applied to a copy of
+    the installed reference: its sinkslot_solve(backend="auto") on CUDA float32
+    tensors runs this backend and returns its result."""
+    code = f"""
+import sys, torch
+sys.path.insert(0, {ROOT!r})
+sys.path.insert(0, {os.path.join(ROOT, "tests")!r})
+from reference_dispatch_patch import patched_copy
+sys.path.insert(0, patched_copy({REF!r}, {str(tmp_path)!r}))
+import sinkslot, sinkslot_b200
+calls = []
+orig = sinkslot_b200.sinkslot_solve
+def spy(*a, **k):
+    calls.append(1)
+    return orig(*a, **k)
+sinkslot_b200.sinkslot_solve = spy
+torch.manual_seed(0)
+X = torch.randn(3000, 3, device="cuda"); Y = torch.randn(2500, 3, device="cuda") + 1
+r = sinkslot.sinkslot_solve(X, Y, eps=0.05, L=16, seed=0, n_iters=50)
+assert calls == [1], calls
+want = orig(X, Y, eps=0.05, L=16, seed=0, n_iters=50)
+assert torch.equal(r.phi, want.phi) and torch.equal(r.rows, want.rows)
+r = sinkslot.sinkslot_solve(X.double(), Y.double(), eps=0.05, L=16, seed=0, n_iters=5,
+                            backend="torch")
+assert calls == [1], "backend='torch' must stay the reference's own path"
+print("dispatch ok")
+"""
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600)
+    assert out.returncode == 0 and "dispatch ok" in out.stdout, out.stdout + out.stderr
+
+
+def test_colour_transfer_shape_matches_reference(cuda, ref):
+    """N = 2^21 source, M = 2^20 target, 16-component mixtures in [0,1]^3,
+    Dirichlet(1) weights, eps = 0.005, L = 128, symmetric (alpha 0.5), marginal
+    stop at 1e-6 every 5 iterations, then the plan and the barycentric map.
+
+    At this size some Dirichlet weights (down to ~1e-13) are below the float32
+    resolution of the slices' cumulative sums, so their points receive no mass
+    in any slice: their rows and columns are empty, their potentials +inf, and
+    the reference's marginal check is NaN at every check -- it never stops
+    before max_iter.  This build reproduces that (same empty segments, same
+    infinities, NaN violation).  max_iter is held to 100 here so the
+    reference's torch loop finishes in seconds."""
+    import bench
+    from sinkslot_b200 import sinkslot_solve, sparse_barycentric_map
+    from sinkslot_b200.sinkhorn_solvers import plan_values
+    w = bench.CONFIGS["cfg3"]
+    x, y, a, b = bench.make_inputs(0, w)
+    X, Y, A, B = (v.to(cuda) for v in (x, y, a, b))
+    kw = dict(eps=w["eps"], L=w["L"], seed=0, stop_mode="marginal", stop_max_iter=100,
+              stop_tol=w["stop_tol"], stop_check_every=w["stop_check_every"],
+              variant="symmetric", alpha=w["alpha"])
+    r_t = ref.sinkslot_solve(X, Y, A, B, backend="torch", **kw)
+    r_tr = ref.sinkslot_solve(X, Y, A, B, backend="triton", **kw)
+    ours = sinkslot_solve(X, Y, A, B, **kw)
+    assert torch.equal(ours.rows, r_t.rows) and torch.equal(ours.cols, r_t.cols)
+    torch.testing.assert_close(ours.S, r_t.S, rtol=3e-7, atol=0)
+    assert ours.iters_run == r_t.iters_run == r_tr.iters_run == 100
+    assert ours.converged is False and r_t.converged is False
+    assert (ours.final_viol != ours.final_viol) and (r_t.final_viol != r_t.final_viol)  # NaN
+    empty_rows = torch.bincount(ours.rows, minlength=X.shape[0]) == 0
+    assert bool(empty_rows.any()) and bool(torch.isinf(ours.phi[empty_rows]).all())
+    _assert_within_noise_floor((ours.phi, ours.psi), (r_tr.phi, r_tr.psi), (r_t.phi, r_t.psi),
+                               "colour-transfer shape")
+    # plan values and the barycentric map on the shared support
+    T = plan_values(ours.phi, ours.psi, ours.rows, ours.cols, ours.S, X, Y, w["eps"])
+    cost = (X[r_t.rows] - Y[r_t.cols]).square().sum(1)
+    T_ref = (r_t.phi[r_t.rows] + r_t.psi[r_t.cols]
+             + r_t.S.clamp_min(torch.finfo(torch.float32).tiny).log() - cost / w["eps"]).exp()
+    fin = torch.isfinite(T_ref)
+    assert torch.equal(torch.isfinite(T), fin)
+    err = (T[fin] - T_ref[fin]).abs() / T_ref[fin].abs().clamp_min(1e-30)
+    assert float(err.median()) < 1e-3
+    Tx, _ = sparse_barycentric_map(T, ours.rows, ours.cols, X, Y)
+    Tx_ref, _ = ref.sparse_barycentric_map(T_ref, r_t.rows, r_t.cols, X, Y)
+    ok = torch.isfinite(Tx_ref).all(1)
+    d = (Tx[ok] - Tx_ref[ok]).abs().max(1).values
+    assert float(d.median()) < 1e-4 and float(torch.quantile(d, 0.99)) < 1e-2

@@ -61,6 +61,31 @@ def test_projection_bits(cuda, oracle, n, d, L, same_as_cublas):
         np.testing.assert_array_equal(got, cublas)
 
 
+@pytest.mark.parametrize("n,d,L,chunk", [
+    (10000, 2, 64, None),        # the CPU-runnable configuration's shape
+    (1 << 18, 2, 100, None),     # gradient flow
+    (1 << 20, 3, 64, None),      # the headline
+    (1 << 20, 3, 64, 8),         # chunked GEMMs
+    (1 << 21, 3, 128, None),     # colour-transfer source cloud
+    (1 << 24, 3, 64, 8),         # scale-out
+    (100003, 4, 48, 5),
+])
+def test_own_projection_equals_cublas_at_workload_shapes(cuda, n, d, L, chunk):
+    """For d <= 4 the support builder projects with its own FMA-chain kernel
+    instead of materialising cuBLAS's `X @ theta.T`: bit-equal to cuBLAS's
+    product at every workload shape, chunk by chunk as the reference issues it
+    (solver.py:219-221)."""
+    from sinkslot_b200.solver import get_random_projections, project
+    X = _points(n, d, 2).to(cuda)
+    th = get_random_projections(d, L, 0).float().to(cuda)
+    got = project(X, th)
+    step = L if chunk is None else chunk
+    for s in range(0, L, step):
+        want = (X @ th[s:s + step].T).T
+        assert torch.equal(got[s:s + step], want), f"slices {s}..{s + step} differ from cuBLAS"
+    del got
+
+
 def test_support_uses_the_reference_gemm_bits(cuda):
     """d = 5 with few points, where cuBLAS's rounding differs from the FMA
     chain: the support still equals the reference op sequence on this device."""

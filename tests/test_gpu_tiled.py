@@ -225,3 +225,31 @@ def test_one_side_tiled_matches_exact(cuda, sides, variant):
     atol_q = ATOL + 2e-7 * float(qe.abs().max())
     torch.testing.assert_close(pt, pe, rtol=RTOL, atol=atol_p)
     torch.testing.assert_close(qt, qe, rtol=RTOL, atol=atol_q)
+
+
+@pytest.mark.parametrize("iters", [1, 2, 3])
+@pytest.mark.parametrize("variant", ["alternating", "symmetric"])
+@pytest.mark.parametrize("kind,eps", [("uniform", 0.01), ("dirichlet", 0.002)])
+def test_first_iterations_tiled_match_exact(cuda, iters, variant, kind, eps):
+    """The first iteration has no previous log-sum-exp to stabilise by: its row
+    half-step (both half-steps, symmetric) gathers the zero start potential and
+    runs the exact kernel without the gather -- the same bits as gathering
+    zeros --, and the alternating first column half-step takes its stabilisers
+    from a tiled max pass.  Both paths are fp32 with different summation
+    orders, so near zero the bar's atol is scaled by max|phi| as in the other
+    tiled-vs-exact comparisons."""
+    from sinkslot_b200.sinkhorn_solvers import (build_tiles, sinkslot_alternating_b200,
+                                                sinkslot_symmetric_b200)
+    n, m = 60000, 50000
+    csr = _problem(n, m, 3, 11, kind, cuda, L=64, eps=eps)
+    tiles = (build_tiles(csr[0], csr[1], csr[2], n, m), build_tiles(csr[3], csr[4], csr[5], m, n))
+    fn = sinkslot_alternating_b200 if variant == "alternating" else sinkslot_symmetric_b200
+    pe, qe, *_ = fn(*csr, iters)
+    pt, qt, *_ = fn(*csr, iters, tiles=tiles)
+    if iters == 1:
+        # exact kernel on both paths, with and without the gather of zeros
+        assert torch.equal(pt, pe)
+        if variant == "symmetric":
+            assert torch.equal(qt, qe)
+    torch.testing.assert_close(pt, pe, rtol=RTOL, atol=ATOL + 2e-7 * float(pe.abs().max()))
+    torch.testing.assert_close(qt, qe, rtol=RTOL, atol=ATOL + 2e-7 * float(qe.abs().max()))

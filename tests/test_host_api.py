@@ -100,3 +100,41 @@ def test_exports_match_reference_names():
     from sinkslot_b200.sinkhorn_solvers import (sinkslot_alternating_triton,
                                                 sinkslot_symmetric_triton)
     assert callable(sinkslot_alternating_triton) and callable(sinkslot_symmetric_triton)
+
+
+def test_batch_assignment_round_robin():
+    from sinkslot_b200.batched import batch_assignment
+    assert batch_assignment(7, 3) == [[0, 3, 6], [1, 4], [2, 5]]
+    assert batch_assignment(2, 4) == [[0], [1], [], []]
+    assert batch_assignment(0, 2) == [[], []]
+    shares = batch_assignment(101, 8)
+    assert sorted(i for s in shares for i in s) == list(range(101))
+    with pytest.raises(ValueError):
+        batch_assignment(3, 0)
+
+
+def test_reference_dispatch_patch_applies(tmp_path):
+    """The maintainer's dispatch edit applies to the installed reference and the
+    patched package still runs its own CPU path (no CUDA here)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ref = os.path.join(root, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "sinkslot")):
+        pytest.skip("the reference package is not installed in baseline/_ref")
+    code = f"""
+import sys, torch
+sys.path.insert(0, {root!r}); sys.path.insert(0, {os.path.join(root, "tests")!r})
+from reference_dispatch_patch import patched_copy
+sys.path.insert(0, patched_copy({ref!r}, {str(tmp_path)!r}))
+import sinkslot
+from sinkslot import sinkhorn_solvers as s
+assert hasattr(s, "_HAS_B200")
+torch.manual_seed(0)
+r = sinkslot.sinkslot_solve(torch.randn(50, 2), torch.randn(40, 2), eps=0.1, L=8, n_iters=5)
+assert r.phi.device.type == "cpu"
+print("ok")
+"""
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and "ok" in out.stdout, out.stdout + out.stderr
