@@ -434,7 +434,7 @@ def run_b200_sharded(args, world, rank, local):
     solver = ShardedSolver(X, Y, A, B, w["eps"], L=w["L"], seed=w["proj_seed"])
     torch.cuda.synchronize(dev)
     setup_ms = (time.perf_counter() - t0) * 1e3
-    nnz = int(solver.rows.numel())
+    nnz = solver.nnz
     solver.solve(max(args.warmup, 0), copy_out=False)
     torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
@@ -819,7 +819,7 @@ def run_cfg5(args):
         from sinkslot_b200.sharded import ShardedSolver
         (solver), setup_ms = _timed(stream, lambda: ShardedSolver(
             X, Y, A, B, w["eps"], L=w["L"], seed=w["proj_seed"], chunk=8))
-        nnz = int(solver.rows.numel())
+        nnz = solver.nnz
         solver.solve(max(args.warmup, 3), copy_out=False)
         sampler = ClockSampler(local) if rank == 0 else None
         if sampler:

@@ -50,11 +50,16 @@ int sinkslot_ot1d_workspace_bytes(int64_t n, int64_t m, int C, int64_t* bytes_ho
  * (R, Cc, mass) triples in the reference's emission order (slice-major, merged
  * position ascending); capacity C * (n + m).  Optional (nullable) outputs: the
  * per-slice argsort permutations ix (C, n) / iy (C, m) as uint32 and the
- * cumsums ca (C, n) / cb (C, m).  *count_host receives the number of triples. */
+ * cumsums ca (C, n) / cb (C, m).  *count_host receives the number of triples.
+ * scan_rows: the cumsums follow the association torch's CUDA scan uses for a
+ * (scan_rows, len) tensor -- 0 means C, the reference's own call; a caller
+ * building some of the slices of a larger batch (one rank of a partitioned
+ * build) passes that batch's slice count, so the bits equal the batch's. */
 int sinkslot_ot1d_batched(const float* PXt, const float* PYt, const float* a, const float* b,
-                          int64_t n, int64_t m, int C, void* workspace, int64_t workspace_bytes,
-                          int64_t* R, int64_t* Cc, float* mass, uint32_t* ix, uint32_t* iy,
-                          float* ca, float* cb, int64_t* count_host, void* stream);
+                          int64_t n, int64_t m, int C, int scan_rows, void* workspace,
+                          int64_t workspace_bytes, int64_t* R, int64_t* Cc, float* mass,
+                          uint32_t* ix, uint32_t* iy, float* ca, float* cb, int64_t* count_host,
+                          void* stream);
 
 int sinkslot_support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chunk,
                                      int64_t* bytes_host);
@@ -80,6 +85,35 @@ int sinkslot_build_support(const float* X, const float* Y, const float* a, const
 int sinkslot_support_export(const void* workspace, int64_t workspace_bytes, int64_t n, int64_t m,
                             int d, int L, int chunk, int64_t nnz, int64_t* rows, int64_t* cols,
                             float* S, void* stream);
+
+/* Support built across the GPUs of a node (one process each, each rank
+ * building a contiguous range of the slices with sinkslot_ot1d_batched).  No
+ * counterpart in the reference, whose support is built on one device
+ * (sot_plan_coo, sinkslot/solver.py:153-232); together they give each rank the
+ * rows of that support it owns, bit-identical to the single-device build. */
+
+int sinkslot_partition_workspace_bytes(int64_t nnz, int64_t* bytes_host);
+
+/* Stable partition of COO entries (seg, other, vals; other / vals nullable) by
+ * the part owning seg: part p holds bounds_host[p] <= seg < bounds_host[p+1]
+ * (host array of parts + 1 non-decreasing values, 1 <= parts <= 64; segments
+ * outside the range go to the nearest end part).  Writes the entries part by
+ * part, each part in input order, and counts_host[p] (host). */
+int sinkslot_partition_coo(const int64_t* seg, const int64_t* other, const float* vals,
+                           int64_t nnz, const int64_t* bounds_host, int parts, void* workspace,
+                           int64_t workspace_bytes, int64_t* seg_out, int64_t* other_out,
+                           float* vals_out, int64_t* counts_host, void* stream);
+
+int sinkslot_coalesce_workspace_bytes(int64_t nraw, int64_t* bytes_host);
+
+/* The coalesce of sot_plan_coo (sinkslot/solver.py:194-232) over raw entries
+ * (R, C, mass) of an n x m problem with L slices: unique keys R * m + C in
+ * ascending order, each key's masses summed in input order, times 1/L.
+ * rows / cols / S need room for nraw entries; *nnz_host receives the count. */
+int sinkslot_coalesce_coo(const int64_t* R, const int64_t* C, const float* mass, int64_t nraw,
+                          int64_t n, int64_t m, int L, void* workspace, int64_t workspace_bytes,
+                          int64_t* rows, int64_t* cols, float* S, int64_t* nnz_host,
+                          void* stream);
 
 int sinkslot_csr_workspace_bytes(int64_t nnz, int64_t nseg, int64_t* bytes_host);
 

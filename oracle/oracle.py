@@ -79,7 +79,8 @@ def lib():
         L.orc_torch_inner_scan_log_tx.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
         L.orc_torch_inner_scan_log_tx.restype = ctypes.c_uint32
         L.orc_ot1d.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
-                               _f32p, _f32p, ctypes.c_int, ctypes.c_int, _i64p, _i64p, _f32p]
+                               _f32p, _f32p, ctypes.c_int, ctypes.c_int, _i64p, _i64p, _f32p,
+                               ctypes.c_int]
         L.orc_ot1d.restype = ctypes.c_int64
         L.orc_coalesce.argtypes = [_i64p, _i64p, _f32p, ctypes.c_int64, ctypes.c_int64,
                                    ctypes.c_int, ctypes.c_int, _i64p, _i64p, _f32p]
@@ -179,9 +180,10 @@ def cumsum(w, C: int, mode: str = "cuda") -> np.ndarray:
 _BUILDERS = {"cuda": (0, 0, 1), "cuda_on_cpu": (1, 0, 0), "cpu": (1, 1, 0)}
 
 
-def ot1d(PXt, PYt, a, b, builder: str = "cuda"):
+def ot1d(PXt, PYt, a, b, builder: str = "cuda", scan_rows: int = 0):
     """Kept (R, C, mass) triples of C slices (solver.py:55-150).  PXt (C, n),
-    PYt (C, m) slice-major projections."""
+    PYt (C, m) slice-major projections.  scan_rows (0: C): the cumsum
+    association of a batch of that many slices."""
     PXt, PYt, a, b = _f32(PXt), _f32(PYt), _f32(a), _f32(b)
     C, n = PXt.shape
     m = PYt.shape[1]
@@ -192,7 +194,8 @@ def ot1d(PXt, PYt, a, b, builder: str = "cuda"):
     cum_mode, emit, _ = _BUILDERS[builder]
     cnt = lib().orc_ot1d(_p(PXt, ctypes.c_float), _p(PYt, ctypes.c_float), n, m, C,
                          _p(a, ctypes.c_float), _p(b, ctypes.c_float), cum_mode, emit,
-                         _p(R, ctypes.c_int64), _p(Cc, ctypes.c_int64), _p(M, ctypes.c_float))
+                         _p(R, ctypes.c_int64), _p(Cc, ctypes.c_int64), _p(M, ctypes.c_float),
+                         int(scan_rows))
     return R[:cnt], Cc[:cnt], M[:cnt]
 
 

@@ -186,8 +186,10 @@ static int64_t ss_right(const float *s, int64_t n, float v) {
 /* ------------------------------------------------------------------------ */
 int64_t orc_ot1d(const float *PXt, const float *PYt, int64_t n, int64_t m, int C,
                  const float *a, const float *b, int cum_mode, int emit_order,
-                 int64_t *R, int64_t *Cc, float *mass_out) {
+                 int64_t *R, int64_t *Cc, float *mass_out, int scan_rows) {
   const int64_t nm = n + m;
+  /* the cumsum association of a batch of scan_rows slices (0: this call's C) */
+  const int scan_c = scan_rows > 0 ? scan_rows : C;
   /* per-slice full arrays (position-major emission needs them all) */
   int64_t *allR = (int64_t *)malloc((size_t)C * nm * sizeof(int64_t));
   int64_t *allC = (int64_t *)malloc((size_t)C * nm * sizeof(int64_t));
@@ -209,8 +211,8 @@ int64_t orc_ot1d(const float *PXt, const float *PYt, int64_t n, int64_t m, int C
       orc_stable_argsort_f32(PYt + (int64_t)c * m, m, iy);
       for (int64_t i = 0; i < n; ++i) wa[i] = a[ix[i]];
       for (int64_t j = 0; j < m; ++j) wb[j] = b[iy[j]];
-      slice_cumsum(wa, n, C, cum_mode, ca, buf);
-      slice_cumsum(wb, m, C, cum_mode, cb, buf);
+      slice_cumsum(wa, n, scan_c, cum_mode, ca, buf);
+      slice_cumsum(wb, m, scan_c, cum_mode, cb, buf);
       /* rank_a = i + searchsorted(cb, ca, right=True); rank_b = j + searchsorted(ca, cb, left) */
       for (int64_t i = 0; i < n; ++i) bounds[i + ss_right(cb, m, ca[i])] = ca[i];
       for (int64_t j = 0; j < m; ++j) bounds[j + ss_left(ca, n, cb[j])] = cb[j];

@@ -31,13 +31,19 @@ P_dbl = ctypes.POINTER(ctypes.c_double)
 _SIGNATURES = {
     "sinkslot_project": [c_vp, c_i64, c_int, c_vp, c_int, c_vp, c_vp],
     "sinkslot_ot1d_workspace_bytes": [c_i64, c_i64, c_int, P_i64],
-    "sinkslot_ot1d_batched": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_i64, c_vp, c_vp,
-                              c_vp, c_vp, c_vp, c_vp, c_vp, P_i64, c_vp],
+    "sinkslot_ot1d_batched": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_int, c_vp, c_i64, c_vp,
+                              c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, P_i64, c_vp],
     "sinkslot_support_workspace_bytes": [c_i64, c_i64, c_int, c_int, c_int, P_i64],
     "sinkslot_build_support": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_vp, c_vp,
                                c_int, c_int, c_vp, c_i64, P_i64, c_vp],
     "sinkslot_support_export": [c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, c_i64, c_vp, c_vp,
                                 c_vp, c_vp],
+    "sinkslot_partition_workspace_bytes": [c_i64, P_i64],
+    "sinkslot_partition_coo": [c_vp, c_vp, c_vp, c_i64, P_i64, c_int, c_vp, c_i64, c_vp, c_vp,
+                               c_vp, P_i64, c_vp],
+    "sinkslot_coalesce_workspace_bytes": [c_i64, P_i64],
+    "sinkslot_coalesce_coo": [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_i64, c_vp,
+                              c_vp, c_vp, P_i64, c_vp],
     "sinkslot_csr_workspace_bytes": [c_i64, c_i64, P_i64],
     "sinkslot_coo_to_csr": [c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_i64, c_vp, c_vp, c_vp,
                             c_vp, P_int, c_vp],

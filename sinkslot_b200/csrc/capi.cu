@@ -34,7 +34,7 @@ extern "C" {
 
 const char* sinkslot_last_error(void) { return last_error(); }
 
-int sinkslot_abi_version(void) { return 100; }
+int sinkslot_abi_version(void) { return 101; }
 
 int sinkslot_project(const float* X, int64_t n, int d, const float* theta, int L, float* out,
                      void* stream) {
@@ -49,14 +49,15 @@ int sinkslot_ot1d_workspace_bytes(int64_t n, int64_t m, int C, int64_t* bytes_ho
 }
 
 int sinkslot_ot1d_batched(const float* PXt, const float* PYt, const float* a, const float* b,
-                          int64_t n, int64_t m, int C, void* workspace, int64_t workspace_bytes,
-                          int64_t* R, int64_t* Cc, float* mass, uint32_t* ix, uint32_t* iy,
-                          float* ca, float* cb, int64_t* count_host, void* stream) {
+                          int64_t n, int64_t m, int C, int scan_rows, void* workspace,
+                          int64_t workspace_bytes, int64_t* R, int64_t* Cc, float* mass,
+                          uint32_t* ix, uint32_t* iy, float* ca, float* cb, int64_t* count_host,
+                          void* stream) {
   g_last_error_clear();
   SINKSLOT_REQUIRE(PXt && PYt && a && b && R && Cc && mass && count_host && workspace,
                    "ot1d_batched: null argument");
-  return ot1d_batched(PXt, PYt, a, b, n, m, C, workspace, (size_t)workspace_bytes, R, Cc, mass, ix,
-                      iy, ca, cb, count_host, ST(stream));
+  return ot1d_batched(PXt, PYt, a, b, n, m, C, scan_rows, workspace, (size_t)workspace_bytes, R,
+                      Cc, mass, ix, iy, ca, cb, count_host, ST(stream));
 }
 
 int sinkslot_support_workspace_bytes(int64_t n, int64_t m, int d, int L, int chunk,
@@ -86,6 +87,44 @@ int sinkslot_support_export(const void* workspace, int64_t workspace_bytes, int6
   SINKSLOT_REQUIRE(workspace && (nnz == 0 || (rows && cols && S)), "support_export: null argument");
   return support_export(workspace, (size_t)workspace_bytes, n, m, d, L, chunk, nnz, rows, cols, S,
                         ST(stream));
+}
+
+int sinkslot_partition_workspace_bytes(int64_t nnz, int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && nnz >= 0, "partition_workspace_bytes: bad args");
+  *bytes_host = (int64_t)partition_workspace_bytes(nnz);
+  return kOk;
+}
+
+int sinkslot_partition_coo(const int64_t* seg, const int64_t* other, const float* vals,
+                           int64_t nnz, const int64_t* bounds_host, int parts, void* workspace,
+                           int64_t workspace_bytes, int64_t* seg_out, int64_t* other_out,
+                           float* vals_out, int64_t* counts_host, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(workspace && (nnz == 0 || (seg && seg_out)) && (!other || other_out) &&
+                       (!vals || vals_out),
+                   "partition_coo: null argument");
+  return partition_coo(seg, other, vals, nnz, bounds_host, parts, workspace,
+                       (size_t)workspace_bytes, seg_out, other_out, vals_out, counts_host,
+                       ST(stream));
+}
+
+int sinkslot_coalesce_workspace_bytes(int64_t nraw, int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && nraw >= 0, "coalesce_workspace_bytes: bad args");
+  *bytes_host = (int64_t)coalesce_workspace_bytes(nraw);
+  return kOk;
+}
+
+int sinkslot_coalesce_coo(const int64_t* R, const int64_t* C, const float* mass, int64_t nraw,
+                          int64_t n, int64_t m, int L, void* workspace, int64_t workspace_bytes,
+                          int64_t* rows, int64_t* cols, float* S, int64_t* nnz_host,
+                          void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(workspace && (nraw == 0 || (R && C && mass && rows && cols && S)),
+                   "coalesce_coo: null argument");
+  return coalesce_coo(R, C, mass, nraw, n, m, L, workspace, (size_t)workspace_bytes, rows, cols,
+                      S, nnz_host, ST(stream));
 }
 
 int sinkslot_csr_workspace_bytes(int64_t nnz, int64_t nseg, int64_t* bytes_host) {

@@ -235,18 +235,20 @@ __global__ void slice_cumsum_seq_kernel(const uint32_t* __restrict__ order,
   }
 }
 
-// torch's scan order for C rows of len (C > 1): chunks of 2*tx elements, tx from
-// torch_inner_scan_log_tx.  `scratch`: C * nchunks * (log_tx + 3) floats, less
-// than C * len since 2 * tx >= 32.
+// torch's scan order for C rows of len: chunks of 2*tx elements, tx from
+// torch_inner_scan_log_tx(scan_rows, len) -- the order torch uses for a
+// (scan_rows, len) tensor, of which these are C rows (scan_rows >= C; a single
+// row is scanned sequentially).  `scratch`: C * nchunks * (log_tx + 3) floats,
+// less than C * len since 2 * tx >= 32.
 static int slice_cumsum(const uint32_t* order, const float* w, float* out, int64_t len, int C,
-                        float* scratch, cudaStream_t stream) {
+                        int scan_rows, float* scratch, cudaStream_t stream) {
   if (len == 0 || C == 0) return kOk;
-  if (C == 1) {
+  if (scan_rows == 1) {
     slice_cumsum_seq_kernel<<<1, 32, 0, stream>>>(order, w, out, len);
     SINKSLOT_CHECK_LAUNCH();
     return kOk;
   }
-  const int log_tx = (int)torch_inner_scan_log_tx((uint32_t)C, (uint32_t)len);
+  const int log_tx = (int)torch_inner_scan_log_tx((uint32_t)scan_rows, (uint32_t)len);
   const int tx = 1 << log_tx;
   const int64_t nchunks = ceil_div64(len, (int64_t)2 * tx);
   SINKSLOT_REQUIRE(nchunks <= 0x7fffffff && C <= 65535, "cumsum: too many chunks or rows");
@@ -502,8 +504,8 @@ static void carve_slices(Carver& cv, SliceBufs& b, int64_t n, int64_t m, int C) 
 // cumsums and count the kept merge entries per tile (exclusive offsets in
 // b.counts, total in *d_total).  Returns the sorted index arrays.
 static int slices_prepare(SliceBufs& b, const float* a, const float* bw, int64_t n, int64_t m,
-                          int C, const uint32_t** IX, const uint32_t** IY, int64_t* d_total,
-                          cudaStream_t stream) {
+                          int C, int scan_rows, const uint32_t** IX, const uint32_t** IY,
+                          int64_t* d_total, cudaStream_t stream) {
   bool alt = false;
   SINKSLOT_TRY(radix_sort_pairs<uint32_t>(b.kx, b.vx, b.kx2, b.vx2, true, C, n, 32, b.hist, b.stmp,
                                           &alt, stream));
@@ -512,8 +514,8 @@ static int slices_prepare(SliceBufs& b, const float* a, const float* bw, int64_t
                                           &alt, stream));
   const uint32_t* iy = alt ? b.vy2 : b.vy;
   // the sort keys are dead once the orders exist: their buffers hold the scan's scratch
-  SINKSLOT_TRY(slice_cumsum(ix, a, b.ca, n, C, reinterpret_cast<float*>(b.kx2), stream));
-  SINKSLOT_TRY(slice_cumsum(iy, bw, b.cb, m, C, reinterpret_cast<float*>(b.ky2), stream));
+  SINKSLOT_TRY(slice_cumsum(ix, a, b.ca, n, C, scan_rows, reinterpret_cast<float*>(b.kx2), stream));
+  SINKSLOT_TRY(slice_cumsum(iy, bw, b.cb, m, C, scan_rows, reinterpret_cast<float*>(b.ky2), stream));
   const int tps = (int)ceil_div64(n + m, kMergeTile);
   merge_count_kernel<<<dim3(tps, C), kMergeThreads, 0, stream>>>(b.ca, b.cb, n, m, tps, b.counts);
   SINKSLOT_CHECK_LAUNCH();
@@ -539,10 +541,12 @@ size_t ot1d_workspace_bytes(int64_t n, int64_t m, int C) {
 }
 
 int ot1d_batched(const float* PXt, const float* PYt, const float* a, const float* b_w, int64_t n,
-                 int64_t m, int C, void* ws, size_t ws_bytes, int64_t* R, int64_t* Cc, float* M,
-                 uint32_t* ix_out, uint32_t* iy_out, float* ca_out, float* cb_out,
-                 int64_t* count_out, cudaStream_t stream) {
+                 int64_t m, int C, int scan_rows, void* ws, size_t ws_bytes, int64_t* R,
+                 int64_t* Cc, float* M, uint32_t* ix_out, uint32_t* iy_out, float* ca_out,
+                 float* cb_out, int64_t* count_out, cudaStream_t stream) {
   SINKSLOT_REQUIRE(n >= 1 && m >= 1 && C >= 1, "ot1d: need n >= 1, m >= 1, C >= 1");
+  if (scan_rows <= 0) scan_rows = C;
+  SINKSLOT_REQUIRE(scan_rows >= C, "ot1d: scan_rows must be 0 or >= C");
   SINKSLOT_REQUIRE(n < (int64_t(1) << 31) && m < (int64_t(1) << 31), "ot1d: n, m must be < 2^31");
   Carver cv(ws, ws_bytes);
   SliceBufs b;
@@ -557,7 +561,7 @@ int ot1d_batched(const float* PXt, const float* PYt, const float* a, const float
   float_keys_kernel<<<grid_for((int64_t)C * m, 256), 256, 0, stream>>>(PYt, (int64_t)C * m, b.ky);
   SINKSLOT_CHECK_LAUNCH();
   const uint32_t *ix, *iy;
-  SINKSLOT_TRY(slices_prepare(b, a, b_w, n, m, C, &ix, &iy, d_total, stream));
+  SINKSLOT_TRY(slices_prepare(b, a, b_w, n, m, C, scan_rows, &ix, &iy, d_total, stream));
   const int tps = (int)ceil_div64(n + m, kMergeTile);
   merge_emit_kernel<false><<<dim3(tps, C), kMergeThreads, 0, stream>>>(
       b.ca, b.cb, ix, iy, n, m, tps, b.counts, 0, R, Cc, M, nullptr, nullptr);
@@ -634,7 +638,7 @@ int build_support(const float* X, const float* Y, const float* a, const float* b
     SINKSLOT_TRY(slice_keys(X, PX, n, d, theta, L, start, C, b.s.kx, stream));
     SINKSLOT_TRY(slice_keys(Y, PY, m, d, theta, L, start, C, b.s.ky, stream));
     const uint32_t *ix, *iy;
-    SINKSLOT_TRY(slices_prepare(b.s, a, bw, n, m, C, &ix, &iy, b.scal, stream));
+    SINKSLOT_TRY(slices_prepare(b.s, a, bw, n, m, C, C, &ix, &iy, b.scal, stream));
     merge_emit_kernel<true><<<dim3(tps, C), kMergeThreads, 0, stream>>>(
         b.s.ca, b.s.cb, ix, iy, n, m, tps, b.s.counts, nraw, nullptr, nullptr, nullptr, b.rkey,
         b.rm);

@@ -166,7 +166,9 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
   g.smem_bytes = pipe_smem((int)R, 1 << logW);
   const int64_t ntiles = (int64_t)g.P * g.B;
-  g.cap = nnz + (2 * kSlab - 1) * ntiles;  // each tile: an odd number of slabs
+  // each tile: an odd number of slabs; then one group of slabs of tail padding,
+  // which a consumer warp's group loads may read past the last tile
+  g.cap = nnz + (2 * kSlab - 1) * ntiles + kGroup * kSlab;
   Carver cv(nullptr, 0);
   cv.take<int64_t>(8);            // header: [0] longest row of <= kMaxTiledRow entries
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
@@ -986,12 +988,25 @@ __device__ __forceinline__ void prefetch_entries(const uint2* ent, int64_t e0, i
 // Lane `lane` of slabs g .. g+kGroup-1 of the tile whose entries start at e0
 // (only the slabs below nsl are loaded): coalesced 8-byte streaming loads, 256
 // bytes per slab.
+#ifndef SINKSLOT_TILE_UNCOND_LOADS
+#define SINKSLOT_TILE_UNCOND_LOADS 0
+#endif
 __device__ __forceinline__ void load_group(const uint2* ent, int64_t e0, int nsl, int g, int lane,
                                            uint2 (&e)[kGroup]) {
   const uint2* p = ent + e0 + (int64_t)g * kSlab + lane;
+#if SINKSLOT_TILE_UNCOND_LOADS
+  // a group that starts inside the tile loads all its slabs: those past the
+  // tile's end (at most kGroup - 1) read the next tile or the layout's tail
+  // padding, a whole group long; process_group ignores them
+  if (g < nsl) {
+#pragma unroll
+    for (int j = 0; j < kGroup; ++j) e[j] = ld_stream(p + j * kSlab);
+  }
+#else
 #pragma unroll
   for (int j = 0; j < kGroup; ++j)
     if (g + j < nsl) e[j] = ld_stream(p + j * kSlab);
+#endif
 }
 
 // The terms of a group of `cnt` (>= 1) slabs; when the whole group exists one

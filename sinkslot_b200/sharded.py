@@ -112,6 +112,150 @@ def drive(run_chunk: Callable[[int, int, int], tuple[float, float]],
     return it, False, value
 
 
+# --------------------------------------------------------------------------
+# the support built across the ranks
+# --------------------------------------------------------------------------
+def slice_range(L: int, world: int, rank: int) -> tuple[int, int]:
+    """Slices [l0, l1) of the L slices that rank builds: contiguous ranges in
+    rank order, so the ranks' entries, taken in rank order, are in slice order."""
+    return rank * L // world, (rank + 1) * L // world
+
+
+def owner_bounds(n: int, world: int) -> list[int]:
+    """world + 1 non-decreasing bounds: rank g owns segments [b[g], b[g+1]),
+    the slices of shard_bounds."""
+    b = []
+    for g in range(world):
+        start, count = shard_bounds(n, world, g)
+        b.append(start if count > 0 else n)
+    return b + [n]
+
+
+def exchange(arrays, counts, group):
+    """All-to-all of equally partitioned arrays: arrays[i] holds, part by part,
+    counts[g] entries for rank g; returns the arrays this rank receives, the
+    parts of ranks 0, 1, ... in that order, and the received counts."""
+    world = dist.get_world_size(group)
+    dev = arrays[0].device
+    send = torch.tensor([int(c) for c in counts], dtype=torch.int64, device=dev)
+    recv = torch.empty(world, dtype=torch.int64, device=dev)
+    dist.all_to_all_single(recv, send, group=group)
+    rc = [int(v) for v in recv.tolist()]
+    out = []
+    for a in arrays:
+        o = torch.empty(sum(rc), dtype=a.dtype, device=dev)
+        dist.all_to_all_single(o, a.contiguous(), rc, [int(c) for c in counts], group=group)
+        out.append(o)
+    return out, rc
+
+
+class DeviceOps:
+    """The device steps of the partitioned support build, in libsinkslot_b200.so."""
+
+    def __init__(self, device):
+        self.dev = device
+
+    def _ws(self, nbytes):
+        return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=self.dev)
+
+    def project_t(self, X, theta):
+        """(C, n) slice-major projections of X onto theta's rows: the FMA chain
+        for d <= 4, cuBLAS's product otherwise (as sot_plan_coo)."""
+        from .solver import OWN_PROJECTION_MAX_D, project
+        if X.shape[1] <= OWN_PROJECTION_MAX_D:
+            return project(X, theta)
+        return (X @ theta.T).T.contiguous()
+
+    def ot1d(self, PXt, PYt, a, b, scan_rows):
+        from .solver import _ot_1d_coo_batched_cuda
+        return _ot_1d_coo_batched_cuda(PXt.T, PYt.T, a, b, scan_rows=scan_rows)
+
+    def partition(self, seg, other, vals, bounds):
+        nnz = seg.numel()
+        nb = _lib.out_i64()
+        call("sinkslot_partition_workspace_bytes", nnz, ctypes.byref(nb))
+        ws = self._ws(nb.value)
+        so, oo, vo = torch.empty_like(seg), torch.empty_like(other), torch.empty_like(vals)
+        parts = len(bounds) - 1
+        bh = (ctypes.c_int64 * (parts + 1))(*bounds)
+        counts = (ctypes.c_int64 * parts)()
+        with torch.cuda.device(self.dev):
+            call("sinkslot_partition_coo", ptr(seg), ptr(other), ptr(vals), nnz, bh, parts,
+                 ptr(ws), ws.numel(), ptr(so), ptr(oo), ptr(vo), counts, stream_of(self.dev))
+        return so, oo, vo, list(counts)
+
+    def coalesce(self, R, Cc, M, n, m, L):
+        nraw = R.numel()
+        nb = _lib.out_i64()
+        call("sinkslot_coalesce_workspace_bytes", nraw, ctypes.byref(nb))
+        ws = self._ws(nb.value)
+        rows = torch.empty(max(nraw, 1), dtype=torch.int64, device=self.dev)
+        cols = torch.empty_like(rows)
+        S = torch.empty(max(nraw, 1), dtype=torch.float32, device=self.dev)
+        k = _lib.out_i64()
+        with torch.cuda.device(self.dev):
+            call("sinkslot_coalesce_coo", ptr(R), ptr(Cc), ptr(M), nraw, n, m, L, ptr(ws),
+                 ws.numel(), ptr(rows), ptr(cols), ptr(S), ctypes.byref(k), stream_of(self.dev))
+        return rows[:k.value], cols[:k.value], S[:k.value]
+
+    def cost_lam(self, X, Y, rows, cols, S, eps):
+        return cost_and_lam(X, Y, rows, cols, S, eps)[0]
+
+
+def build_partitioned_support(X, Y, a, b, eps, L: int, seed: int, chunk, group, ops=None):
+    """This rank's part of the sliced support, built across the ranks of `group`
+    (every rank holds the same X, Y, a, b):
+
+    1. rank g builds the raw entries of slices slice_range(L, world, g)
+       (reference: _ot_1d_coo_batched_cuda, solver.py:107-150), each slice
+       with the cumsum association of the batch (`chunk` slices, or all L) that
+       holds it in the single-device build;
+    2. the entries go to their row's owner (stable partition + all-to-all),
+       where they arrive in slice order;
+    3. each owner coalesces its rows (solver.py:194-232: duplicates summed in
+       slice order, / L) -- the same bits as the single-device build -- and
+       computes lam = log S - cost / eps for them;
+    4. the coalesced entries go to their column's owner, arriving in row order.
+
+    Returns (rows, cols, S, lam) of the rows this rank owns, sorted by
+    rows * m + cols, and (cols, rows, lam) of the columns it owns, in row
+    order within each column's run of the concatenation."""
+    from .solver import get_random_projections
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    ops = ops if ops is not None else DeviceOps(X.device)
+    n, d = X.shape
+    m = Y.shape[0]
+    theta = get_random_projections(d, L, seed).to(X.dtype).to(X.device)
+    l0, l1 = slice_range(L, world, rank)
+    step = L if chunk is None else max(1, min(L, int(chunk)))
+    parts = []
+    for b0 in range(0, L, step):  # the single-device build's batches
+        b1 = min(L, b0 + step)
+        s0, s1 = max(b0, l0), min(b1, l1)
+        if s0 >= s1:
+            continue
+        t = theta[s0:s1].contiguous()
+        parts.append(ops.ot1d(ops.project_t(X, t), ops.project_t(Y, t), a, b, b1 - b0))
+    if parts:
+        R = torch.cat([p[0] for p in parts])
+        Cc = torch.cat([p[1] for p in parts])
+        M = torch.cat([p[2] for p in parts])
+    else:
+        R = torch.zeros(0, dtype=torch.int64, device=X.device)
+        Cc = torch.zeros(0, dtype=torch.int64, device=X.device)
+        M = torch.zeros(0, dtype=torch.float32, device=X.device)
+    del parts
+    R, Cc, M, counts = ops.partition(R, Cc, M, owner_bounds(n, world))
+    (R, Cc, M), _ = exchange([R, Cc, M], counts, group)
+    rows, cols, S = ops.coalesce(R, Cc, M, n, m, L)
+    del R, Cc, M
+    lam = ops.cost_lam(X, Y, rows, cols, S, eps)
+    c_cols, c_rows, c_lam, counts = ops.partition(cols, rows, lam, owner_bounds(m, world))
+    (c_cols, c_rows, c_lam), _ = exchange([c_cols, c_rows, c_lam], counts, group)
+    return (rows, cols, S, lam), (c_cols, c_rows, c_lam)
+
+
 def _reduce_max_dist(group, device):
     def reduce_max(c0: float, c1: float) -> tuple[float, float]:
         nan = [math.isnan(c0), math.isnan(c1)]
@@ -188,7 +332,7 @@ class ShardedSolver:
     zero potentials; ``close`` unmaps the peers' buffers (collective)."""
 
     def __init__(self, X, Y, a, b, eps, L=64, seed=0, chunk=None, variant="alternating",
-                 alpha=0.5, group=None, tiled: bool = True):
+                 alpha=0.5, group=None, tiled: bool = True, support: str = "partitioned"):
         if not dist.is_initialized():
             raise RuntimeError("sharded solves need torch.distributed initialised")
         self.group = group
@@ -201,20 +345,40 @@ class ShardedSolver:
         n, m = X.shape[0], Y.shape[0]
         self.n, self.m = n, m
         self.eps, self.alpha, self.variant = eps, alpha, variant
-        self.rows, self.cols, self.S = sot_plan_coo(X, Y, a, b, L=L, seed=seed, chunk=chunk)
-        sizes = [None] * self.world
-        dist.all_gather_object(sizes, (n, m, self.rows.numel()), group=group)
-        if any(s != sizes[0] for s in sizes):
-            raise ValueError(f"ranks built different supports {sizes}: inputs must be identical")
-        lam, _ = cost_and_lam(X, Y, self.rows, self.cols, self.S, eps)
         self.log_a, self.log_b = a.log().contiguous(), b.log().contiguous()
-        r_ptr, r_idx, r_lam, _ = _to_csr(self.rows, self.cols, lam, n, want_perm=False)
-        c_ptr, c_idx, c_lam, _ = _to_csr(self.cols, self.rows, lam, m, want_perm=False)
         self.r0, self.nr = shard_bounds(n, self.world, self.rank)
         self.c0, self.nc = shard_bounds(m, self.world, self.rank)
-        self.row = slice_csr(r_ptr, r_idx, r_lam, self.r0, self.nr)
-        self.col = slice_csr(c_ptr, c_idx, c_lam, self.c0, self.nc)
-        del r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, lam
+        sizes = [None] * self.world
+        dist.all_gather_object(sizes, (n, m, X.shape[1], L, seed), group=group)
+        if any(s != sizes[0] for s in sizes):
+            raise ValueError(f"ranks were given different problems {sizes}")
+        if support == "partitioned":
+            # each rank builds a range of the slices; the entries meet at their
+            # row and column owners (build_partitioned_support)
+            (rows, cols, S, lam), (c_cols, c_rows, c_lam) = build_partitioned_support(
+                X, Y, a, b, eps, L, seed, chunk, group)
+            # this rank's rows of the support (sorted by rows * m + cols)
+            self.rows, self.cols, self.S = rows, cols, S
+            p, i, v, _ = _to_csr(rows - self.r0, cols, lam, self.nr, want_perm=False)
+            self.row = (p, i, v, int(i.numel()))
+            p, i, v, _ = _to_csr(c_cols - self.c0, c_rows, c_lam, self.nc, want_perm=False)
+            self.col = (p, i, v, int(i.numel()))
+            del rows, cols, S, lam, c_cols, c_rows, c_lam
+        elif support == "replicated":
+            # every rank builds the whole support and keeps its slices
+            self.rows, self.cols, self.S = sot_plan_coo(X, Y, a, b, L=L, seed=seed, chunk=chunk)
+            lam, _ = cost_and_lam(X, Y, self.rows, self.cols, self.S, eps)
+            r_ptr, r_idx, r_lam, _ = _to_csr(self.rows, self.cols, lam, n, want_perm=False)
+            c_ptr, c_idx, c_lam, _ = _to_csr(self.cols, self.rows, lam, m, want_perm=False)
+            self.row = slice_csr(r_ptr, r_idx, r_lam, self.r0, self.nr)
+            self.col = slice_csr(c_ptr, c_idx, c_lam, self.c0, self.nc)
+            del r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, lam
+        else:
+            raise ValueError(f"support must be 'partitioned' or 'replicated', got {support!r}")
+        self.support = support
+        t = torch.tensor([self.row[3]], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, group=group)
+        self.nnz = int(t.item())  # entries of the whole support
         self.r_tiles = build_tiles(self.row[0], self.row[1], self.row[2], self.nr, m) \
             if tiled and tiles_pay_off(self.nr, m, self.row[3]) else None
         self.c_tiles = build_tiles(self.col[0], self.col[1], self.col[2], self.nc, n) \
@@ -284,11 +448,15 @@ def sinkslot_solve_sharded(X, Y, a=None, b=None, eps=0.05, L=64, seed=0, n_iters
                            stop_mode="fixed", stop_max_iter=20000, stop_tol=1e-6,
                            stop_check_every=5, chunk=None, backend="auto",
                            variant="alternating", alpha=0.5, group=None,
-                           tiled: bool = True) -> SinkslotSolveResult:
-    """``sinkslot_solve`` with the Sinkhorn loop partitioned over the ranks of
-    ``group`` (default: the world), one GPU each.  Same arguments and result
-    as ``sinkslot_solve`` (every rank returns the full phi, psi and support);
-    X, Y, a, b must be identical on every rank."""
+                           tiled: bool = True, support: str = "partitioned",
+                           gather_support: bool = True) -> SinkslotSolveResult:
+    """``sinkslot_solve`` with the support build and the Sinkhorn loop
+    partitioned over the ranks of ``group`` (default: the world), one GPU
+    each.  Same arguments and result as ``sinkslot_solve``: every rank returns
+    the full phi, psi and -- with ``gather_support`` (default) -- the full
+    support; without it, the rows of the support it owns.  X, Y, a, b must be
+    identical on every rank.  ``support="replicated"`` has every rank build the
+    whole support instead of its share."""
     if not dist.is_initialized():
         raise RuntimeError("sinkslot_solve_sharded needs torch.distributed initialised")
     if a is None:
@@ -302,11 +470,28 @@ def sinkslot_solve_sharded(X, Y, a=None, b=None, eps=0.05, L=64, seed=0, n_iters
     if mode == "potential" and eps is None:
         raise ValueError("eps is required for stop.mode == 'potential'")
     solver = ShardedSolver(X, Y, a, b, eps, L=L, seed=seed, chunk=chunk, variant=variant,
-                           alpha=alpha, group=group, tiled=tiled)
+                           alpha=alpha, group=group, tiled=tiled, support=support)
     try:
         phi, psi, it, converged, viol = solver.solve(n_iters, mode, stop_max_iter, stop_tol,
                                                      stop_check_every)
     finally:
         solver.close()
-    return SinkslotSolveResult(phi, psi, solver.rows, solver.cols, solver.S, it, converged,
-                               viol)
+    rows, cols, S = solver.rows, solver.cols, solver.S
+    if gather_support and solver.support == "partitioned":
+        rows, cols, S = (_gather_parts(t, group) for t in (rows, cols, S))
+    return SinkslotSolveResult(phi, psi, rows, cols, S, it, converged, viol)
+
+
+def _gather_parts(t: torch.Tensor, group) -> torch.Tensor:
+    """The ranks' pieces of a 1-D tensor, concatenated in rank order, on every rank."""
+    world = dist.get_world_size(group)
+    n = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
+    sizes = torch.empty(world, dtype=torch.int64, device=t.device)
+    dist.all_gather_into_tensor(sizes, n, group=group)
+    sizes = [int(v) for v in sizes.tolist()]
+    cap = max(sizes) if sizes else 0
+    buf = torch.zeros(cap, dtype=t.dtype, device=t.device)
+    buf[:t.numel()] = t
+    out = torch.empty(world * cap, dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, buf, group=group)
+    return torch.cat([out[g * cap:g * cap + sizes[g]] for g in range(world)])

@@ -75,12 +75,14 @@ def project(X: torch.Tensor, theta: torch.Tensor) -> torch.Tensor:
 
 
 def _ot_1d_coo_batched_cuda(PX: torch.Tensor, PY: torch.Tensor, a: torch.Tensor,
-                            b: torch.Tensor, return_intermediates: bool = False):
+                            b: torch.Tensor, return_intermediates: bool = False,
+                            scan_rows: int = 0):
     """1-D optimal plans of C slices as flat COO (reference: solver.py:107-150).
 
     PX (n, C), PY (m, C).  Returns (rows, cols, vals) of the kept entries in the
     reference's emission order (slice-major).  With ``return_intermediates`` also
-    returns (ix, iy, ca, cb) in the (C, len) layout.
+    returns (ix, iy, ca, cb) in the (C, len) layout.  ``scan_rows`` (0: C)
+    selects the cumsum association of a batch of that many slices.
     """
     dev = _require_cuda_f32("_ot_1d_coo_batched_cuda", PX, PY, a, b)
     n, C = PX.shape
@@ -102,7 +104,8 @@ def _ot_1d_coo_batched_cuda(PX: torch.Tensor, PY: torch.Tensor, a: torch.Tensor,
                  torch.empty((C, m), dtype=torch.float32, device=dev))
     cnt = _lib.out_i64()
     with torch.cuda.device(dev):
-        call("sinkslot_ot1d_batched", ptr(PXt), ptr(PYt), ptr(a), ptr(b), n, m, C, ptr(ws),
+        call("sinkslot_ot1d_batched", ptr(PXt), ptr(PYt), ptr(a), ptr(b), n, m, C, int(scan_rows),
+             ptr(ws),
              ws.numel(), ptr(R), ptr(Cc), ptr(M),
              *(ptr(t) for t in (inter if inter else (None,) * 4)), ctypes.byref(cnt),
              stream_of(dev))

@@ -72,26 +72,48 @@ def _gauge(p, q, p_ref, q_ref):
 
 
 def _disagreement(p, q, p_ref, q_ref):
-    """(count outside rtol/atol, largest deviation) after removing the shift."""
+    """(count outside rtol/atol, largest deviation in units of the rtol/atol
+    bar) after removing the shift."""
     c = _gauge(p, q, p_ref, q_ref)
     count, worst = 0, 0.0
     for u, v, s in ((p, p_ref, c), (q, q_ref, -c)):
         fin = torch.isfinite(v)
         assert torch.equal(torch.isfinite(u), fin), "non-finite pattern differs"
         d = (u.double() - v.double() - s)[fin].abs()
-        count += int((d > ATOL + RTOL * v.double()[fin].abs()).sum())
-        worst = max(worst, float(d.max()) if d.numel() else 0.0)
+        e = d / (ATOL + RTOL * v.double()[fin].abs())
+        count += int((e > 1).sum())
+        worst = max(worst, float(e.max()) if e.numel() else 0.0)
     return count, worst
 
 
 def _assert_within_noise_floor(ours, triton, torch_ref, name):
+    """At most 2x (+16) as many potentials outside the bar as the reference's
+    Triton backend has against its torch backend, none further outside than
+    4x the larger of the bar and Triton's worst."""
     n_ours, w_ours = _disagreement(ours[0], ours[1], torch_ref[0], torch_ref[1])
     n_tri, w_tri = _disagreement(triton[0], triton[1], torch_ref[0], torch_ref[1])
     assert n_ours <= 2 * n_tri + 16, \
         f"{name}: {n_ours} potentials outside rtol/atol (reference Triton vs torch: {n_tri})"
-    assert w_ours <= 2 * w_tri + ATOL, \
-        f"{name}: max deviation {w_ours:.3e} (reference Triton vs torch: {w_tri:.3e})"
+    assert w_ours <= 4 * max(w_tri, 1.0), \
+        f"{name}: worst {w_ours:.2f}x the bar (reference Triton vs torch: {w_tri:.2f}x)"
     return n_ours, n_tri
+
+
+def _assert_as_accurate(mine, theirs, truth, name):
+    """Against the float64 iteration on the same inputs (each solution's
+    shift removed): max and 99.9th-percentile errors no worse than 1.5x the
+    reference torch backend's own."""
+    for u, v, t in ((mine[0], theirs[0], truth[0]), (mine[1], theirs[1], truth[1])):
+        fin = torch.isfinite(t)
+        e_m = (u.double() - t)[fin]
+        e_r = (v.double() - t)[fin]
+        e_m = (e_m - e_m.median()).abs()
+        e_r = (e_r - e_r.median()).abs()
+        q = torch.tensor([0.999], device=t.device, dtype=torch.float64)
+        assert float(e_m.max()) <= 1.5 * float(e_r.max()) + ATOL, \
+            f"{name}: max error {float(e_m.max()):.3e} vs reference {float(e_r.max()):.3e}"
+        qm, qr = float(torch.quantile(e_m[::4], q)), float(torch.quantile(e_r[::4], q))
+        assert qm <= 1.5 * qr + ATOL, f"{name}: p99.9 error {qm:.3e} vs reference {qr:.3e}"
 
 
 def _gauss(n, m, d, seed, shift, weights="uniform"):
@@ -163,6 +185,19 @@ def test_fixed_solves_match_reference(cuda, ref, case, variant):
     assert ours.iters_run == r_t.iters_run == iters
     _assert_within_noise_floor((ours.phi, ours.psi), (r_tr.phi, r_tr.psi), (r_t.phi, r_t.psi),
                                f"{case} {variant}")
+    # the float64 iteration of the reference's torch loop on the same inputs
+    from sinkslot import sinkhorn_solvers as rss
+    from sinkslot import solver as rs
+    A = t[2] if t[2] is not None else torch.full((n,), 1.0 / n, device=cuda)
+    B = t[3] if t[3] is not None else torch.full((m,), 1.0 / m, device=cuda)
+    cost = rs.sparse_sqeuclidean_cost(t[0], t[1], r_t.rows, r_t.cols, use_triton=False)
+    lam = (r_t.S.clamp_min(torch.finfo(torch.float32).tiny).log() - cost / eps).double()
+    loop = rss.sinkslot_alternating_torch if variant == "alternating" else \
+        rss.sinkslot_symmetric_torch
+    phi64, psi64, *_ = loop(r_t.rows, r_t.cols, lam, A.double().log(), B.double().log(), n, m,
+                            iters)
+    _assert_as_accurate((ours.phi, ours.psi), (r_t.phi, r_t.psi), (phi64, psi64),
+                        f"{case} {variant}")
 
 
 @pytest.mark.parametrize("variant", ["alternating", "symmetric"])

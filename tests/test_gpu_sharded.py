@@ -1,6 +1,8 @@
 """The row/column-partitioned solve on two or more GPUs of one node against the
 single-GPU solve of the same problem (one process per GPU, NCCL for set-up
-and stop checks, peer stores for the potentials).
+and stop checks, peer stores for the potentials).  The support, built across
+the ranks (each builds a range of the slices; entries meet at their row and
+column owners), equals the single build bit for bit.
 
 Tolerance: rtol 1e-4 / atol scaled like the tiled-vs-exact comparison (the
 ranks' tiled layouts cut the rows into different panels, so the exact pass
@@ -67,9 +69,14 @@ def _rank(rank, world, port, q):
                       stop_tol=1e-5, stop_check_every=5, variant=variant)
             rs = sinkslot_solve_sharded(x, y, a, b, **kw)
             r1 = sinkslot_solve(x, y, a, b, **kw) if rank == 0 else None
+            sup = (rs.rows.cpu(), rs.cols.cpu(), rs.S.cpu())
+            if r1 is not None:
+                # the support built across the ranks is the single build, bit for bit
+                assert torch.equal(rs.rows, r1.rows) and torch.equal(rs.cols, r1.cols)
+                assert torch.equal(rs.S, r1.S)
             out.append((rs.phi.cpu(), rs.psi.cpu(), rs.iters_run, rs.converged, rs.final_viol,
                         None if r1 is None else (r1.phi.cpu(), r1.psi.cpu(), r1.iters_run,
-                                                 r1.converged, r1.final_viol)))
+                                                 r1.converged, r1.final_viol), sup))
         q.put((rank, out, None))
     except Exception as e:  # reported by the parent
         q.put((rank, None, repr(e)))
@@ -99,7 +106,8 @@ def test_sharded_solve_matches_single_gpu(world):
     for ci, (n, m, variant, mode, eps, L) in enumerate(CASES):
         single = res[0][ci][5]
         for rank in range(world):
-            phi, psi, it, conv, viol, _ = res[rank][ci]
+            phi, psi, it, conv, viol, _, sup = res[rank][ci]
+            assert all(torch.equal(u, v) for u, v in zip(sup, res[0][ci][6]))
             sphi, spsi, sit, sconv, sviol = single
             if mode == "fixed":
                 assert it == sit

@@ -260,3 +260,99 @@ def test_a_rank_that_leaves_between_chunks_is_an_error_on_the_others():
         p.join(timeout=60)
     assert got[1].startswith("error RuntimeError")
     assert got[0].startswith("error"), got[0]
+
+
+class _OracleOps:
+    """The device steps of build_partitioned_support, done by the oracle on CPU."""
+
+    def project_t(self, X, theta):
+        from oracle import oracle
+        return torch.from_numpy(oracle.project(X.numpy(), theta.numpy()))
+
+    def ot1d(self, PXt, PYt, a, b, scan_rows):
+        from oracle import oracle
+        R, C, M = oracle.ot1d(PXt.numpy(), PYt.numpy(), a.numpy(), b.numpy(), builder="cuda",
+                              scan_rows=scan_rows)
+        return torch.from_numpy(R), torch.from_numpy(C), torch.from_numpy(M)
+
+    def partition(self, seg, other, vals, bounds):
+        s = seg.numpy()
+        part = np.searchsorted(np.asarray(bounds[1:-1]), s, side="right")
+        order = np.argsort(part, kind="stable")
+        counts = np.bincount(part, minlength=len(bounds) - 1).tolist()
+        return seg[order], other[order], vals[order], counts
+
+    def coalesce(self, R, C, M, n, m, L):
+        from oracle import oracle
+        r, c, S = oracle.coalesce(R.numpy(), C.numpy(), M.numpy(), m, L, builder="cuda")
+        return torch.from_numpy(r), torch.from_numpy(c), torch.from_numpy(S)
+
+    def cost_lam(self, X, Y, rows, cols, S, eps):
+        from oracle import oracle
+        cost = oracle.sqeuclid_cost(X.numpy(), Y.numpy(), rows.numpy(), cols.numpy())
+        return torch.from_numpy(oracle.lam_values(S.numpy(), cost, eps))
+
+
+def _support_problem():
+    rng = np.random.default_rng(5)
+    n, m = 130, 97
+    x = rng.standard_normal((n, 3)).astype(np.float32)
+    y = (rng.standard_normal((m, 3)) + 0.7).astype(np.float32)
+    a = (rng.random(n) + 0.1).astype(np.float32)
+    b = (rng.random(m) + 0.1).astype(np.float32)
+    return x, y, a / a.sum(), b / b.sum(), 12, 0.05
+
+
+def _support_rank_main(rank, world, port, chunk, q):
+    from sinkslot_b200.sharded import build_partitioned_support
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, y, a, b, L, eps = _support_problem()
+        t = [torch.from_numpy(v) for v in (x, y, a, b)]
+        (rows, cols, S, lam), (cc, cr, cl) = build_partitioned_support(
+            *t, eps, L, 0, chunk, None, ops=_OracleOps())
+        q.put((rank, rows.numpy(), cols.numpy(), S.numpy(), lam.numpy(), cc.numpy(),
+               cr.numpy(), cl.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,chunk", [(2, None), (3, 2), (4, 1), (3, 5), (2, 7)])
+def test_partitioned_support_equals_the_single_build(world, chunk):
+    """Slices built on different ranks, entries routed to their row owners
+    (all-to-all), coalesced there, then routed to their column owners: every
+    rank's rows equal the single build's rows (rows, cols and S bit-exact, in
+    key order), and its columns' entries arrive in the CSC order of the single
+    build."""
+    from oracle import oracle
+    from sinkslot_b200.sharded import owner_bounds
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_support_rank_main, args=(r, world, port, chunk, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict((r[0], r[1:]) for r in (q.get(timeout=120) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, y, a, b, L, eps = _support_problem()
+    rows, cols, S = oracle.sot_plan_coo(x, y, a, b, L, 0, chunk=chunk, builder="cuda")
+    lam = oracle.lam_values(S, oracle.sqeuclid_cost(x, y, rows, cols), eps)
+    rb, cb = owner_bounds(len(x), world), owner_bounds(len(y), world)
+    order = np.argsort(cols, kind="stable")  # CSC order of the single build
+    for g in range(world):
+        r, c, s, lm, cc, cr, cl = got[g]
+        mine = (rows >= rb[g]) & (rows < rb[g + 1])
+        np.testing.assert_array_equal(r, rows[mine])
+        np.testing.assert_array_equal(c, cols[mine])
+        np.testing.assert_array_equal(s, S[mine])
+        np.testing.assert_array_equal(lm, lam[mine])
+        colmine = order[(cols[order] >= cb[g]) & (cols[order] < cb[g + 1])]
+        o = np.argsort(cc, kind="stable")
+        np.testing.assert_array_equal(cc[o], cols[colmine])
+        np.testing.assert_array_equal(cr[o], rows[colmine])
+        np.testing.assert_array_equal(cl[o], lam[colmine])
