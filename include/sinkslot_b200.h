@@ -307,6 +307,25 @@ int sinkslot_barycentric(const float* T, const int64_t* rows, const int64_t* col
                          const float* a, float* Tx, float* Ty, float* grad, void* workspace,
                          int64_t workspace_bytes, void* stream);
 
+int sinkslot_hvp_workspace_bytes(int64_t n, int64_t m, int64_t* bytes_host);
+
+/* Hessian-vector product out = H(X) v of grad_X SLOT_eps on a frozen support:
+ * replaces `hvp_x_sqeuclid_from_potentials` (sinkslot/hvp.py:34-113), whose
+ * linear solve goes through torchsparsegradutils' MINRES.  The plan T is given
+ * by rows (r_ptr, r_idx, r_T: CSR, n rows) and by columns (c_ptr, c_idx, c_T:
+ * CSC, m columns); idx_bytes 2 or 4.  Solves [[diag(a + tau2), P], [P^T,
+ * diag(b + tau2)]] [u; w] = rhs by MINRES on the device until the residual is
+ * at most tol * ||rhs|| or max_iter iterations (the reference passes a for b:
+ * one marginal for both clouds).  x (n, d), y (m, d), v (n, d) fp32, d <= 16.
+ * sol_out (nullable, n + m) receives (u, w); *iters_host the iterations run,
+ * *resid_host the final relative residual. */
+int sinkslot_hvp(const float* x, const float* y, int d, const float* v, const float* a,
+                 const float* b, const int32_t* r_ptr, const void* r_idx, const float* r_T,
+                 const int32_t* c_ptr, const void* c_idx, const float* c_T, int idx_bytes,
+                 int64_t n, int64_t m, double eps, double tau2, double tol, int64_t max_iter,
+                 void* workspace, int64_t workspace_bytes, float* out, float* sol_out,
+                 int64_t* iters_host, double* resid_host, void* stream);
+
 /* dual value <phi, a> + <psi, b> accumulated in fp64 into out[0] (device);
  * the caller multiplies by eps (sinkslot/samples_loss.py:74). */
 int sinkslot_dual_value(const float* phi, const float* a, int64_t n, const float* psi,

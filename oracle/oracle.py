@@ -437,3 +437,83 @@ def samples_loss_value(phi, psi, a, b, eps: float) -> float:
     pa = (_f32(phi) * _f32(a)).astype(np.float32)
     pb = (_f32(psi) * _f32(b)).astype(np.float32)
     return float(np.float32(eps) * np.float32(pa.sum(dtype=np.float64) + pb.sum(dtype=np.float64)))
+
+
+def minres(matvec, b, tol: float = 1e-11, max_iter: int = 8000):
+    """MINRES (Paige & Saunders, 1975) for a symmetric operator, float64: the
+    recurrence the device solver restates (Lanczos vectors, Givens rotations of
+    the tridiagonal, direction vectors; |eta| is the residual norm).  Returns
+    (x, iterations, relative residual).  Stops when |eta| <= tol * ||b||."""
+    b = np.asarray(b, dtype=np.float64)
+    beta1 = float(np.linalg.norm(b))
+    x = np.zeros_like(b)
+    if beta1 == 0.0:
+        return x, 0, 0.0
+    v_prev = np.zeros_like(b)
+    v = b / beta1
+    w1 = np.zeros_like(b)  # w_{k-1}
+    w2 = np.zeros_like(b)  # w_{k-2}
+    beta, c1, s1, c2, s2, eta = beta1, 1.0, 0.0, 1.0, 0.0, beta1
+    k = 0
+    while k < max_iter:
+        k += 1
+        p = matvec(v) - beta * v_prev
+        alpha = float(v @ p)
+        p = p - alpha * v
+        beta_next = float(np.linalg.norm(p))
+        eps_k = s2 * beta
+        dbar = c2 * beta
+        delta = c1 * dbar + s1 * alpha
+        gbar = -s1 * dbar + c1 * alpha
+        gamma = float(np.hypot(gbar, beta_next))
+        if gamma == 0.0:
+            break
+        c, s = gbar / gamma, beta_next / gamma
+        w = (v - eps_k * w2 - delta * w1) / gamma
+        x = x + c * eta * w
+        eta = -s * eta
+        w2, w1 = w1, w
+        c2, s2, c1, s1 = c1, s1, c, s
+        if beta_next == 0.0 or abs(eta) <= tol * beta1:
+            break
+        v_prev, v, beta = v, p / beta_next, beta_next
+    return x, k, abs(eta) / beta1
+
+
+def hvp_system(X, Y, a, v, rows, cols, T, eps: float, tau2: float = 3e-7):
+    """The linear system of hvp.py:84-104 (float64): (M dense, rhs, dlam)."""
+    X = np.asarray(X, np.float64); Y = np.asarray(Y, np.float64)
+    a = np.asarray(a, np.float64); v = np.asarray(v, np.float64)
+    T = np.asarray(T, np.float64); rows = _i64(rows); cols = _i64(cols)
+    n, m = X.shape[0], Y.shape[0]
+    dlam = -(2.0 / eps) * ((X[rows] - Y[cols]) * v[rows]).sum(1)
+    rhs = np.zeros(n + m)
+    np.add.at(rhs, rows, -(T * dlam))
+    np.add.at(rhs, n + cols, -(T * dlam))
+    M = np.zeros((n + m, n + m))
+    M[np.arange(n), np.arange(n)] = a + tau2
+    M[n + np.arange(m), n + np.arange(m)] = a[:m] + tau2  # the reference: a for both blocks
+    np.add.at(M, (rows, n + cols), T)
+    np.add.at(M, (n + cols, rows), T)
+    return M, rhs, dlam
+
+
+def hvp_x_sqeuclid_from_potentials(X, Y, a, v, rows, cols, T, eps: float, tau2: float = 3e-7,
+                                   solver: str = "dense"):
+    """hvp.py:34-113 in float64 with the linear system solved exactly
+    (``solver="dense"``: the point MINRES converges to) or by :func:`minres`.
+    Small problems only (dense (n+m)^2 matrix)."""
+    M, rhs, dlam = hvp_system(X, Y, a, v, rows, cols, T, eps, tau2)
+    if solver == "dense":
+        sol = np.linalg.solve(M, rhs)
+    else:
+        sol, _, _ = minres(lambda z: M @ z, rhs)
+    X = np.asarray(X, np.float64); Y = np.asarray(Y, np.float64)
+    a = np.asarray(a, np.float64); v = np.asarray(v, np.float64)
+    rows = _i64(rows); cols = _i64(cols)
+    n = X.shape[0]
+    u, w = sol[:n], sol[n:]
+    weight = np.asarray(T, np.float64) * (u[rows] + w[cols] + dlam)
+    dT = np.zeros_like(X)
+    np.add.at(dT, rows, weight[:, None] * Y[cols])
+    return 2.0 * a[:, None] * v - 2.0 * dT

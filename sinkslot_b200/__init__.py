@@ -23,6 +23,7 @@ from .gradient import (
     slot_grad,
     sparse_barycentric_map,
 )
+from .hvp import hvp_x_sqeuclid, hvp_x_sqeuclid_from_potentials
 from .samples_loss import SamplesLoss
 from .batched import sinkslot_solve_batched
 from ._lib import LIB_PATH, SinkslotError, lib as load_library
@@ -39,6 +40,8 @@ __all__ = [
     "SinkslotSolveResult",
     "slot_grad",
     "sparse_barycentric_map",
+    "hvp_x_sqeuclid",
+    "hvp_x_sqeuclid_from_potentials",
     "SamplesLoss",
     "sinkslot_solve_batched",
     "SinkslotError",

@@ -78,6 +78,10 @@ _SIGNATURES = {
     "sinkslot_barycentric": [c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_int, c_vp, c_vp,
                              c_vp, c_vp, c_vp, c_i64, c_vp],
     "sinkslot_dual_value": [c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp],
+    "sinkslot_hvp_workspace_bytes": [c_i64, c_i64, P_i64],
+    "sinkslot_hvp": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
+                     c_i64, c_i64, c_dbl, c_dbl, c_dbl, c_i64, c_vp, c_i64, c_vp, c_vp, P_i64,
+                     P_dbl, c_vp],
 }
 
 

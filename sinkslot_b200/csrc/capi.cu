@@ -5,6 +5,7 @@
 #include "../../include/sinkslot_b200.h"
 #include "common.cuh"
 #include "export.h"
+#include "hvp.h"
 #include "primitives.h"
 #include "sinkhorn.h"
 #include "support.h"
@@ -125,6 +126,32 @@ int sinkslot_coalesce_coo(const int64_t* R, const int64_t* C, const float* mass,
                    "coalesce_coo: null argument");
   return coalesce_coo(R, C, mass, nraw, n, m, L, workspace, (size_t)workspace_bytes, rows, cols,
                       S, nnz_host, ST(stream));
+}
+
+int sinkslot_hvp_workspace_bytes(int64_t n, int64_t m, int64_t* bytes_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(bytes_host && n >= 0 && m >= 0, "hvp_workspace_bytes: bad args");
+  *bytes_host = (int64_t)hvp_workspace_bytes(n, m);
+  return kOk;
+}
+
+int sinkslot_hvp(const float* x, const float* y, int d, const float* v, const float* a,
+                 const float* b, const int32_t* r_ptr, const void* r_idx, const float* r_T,
+                 const int32_t* c_ptr, const void* c_idx, const float* c_T, int idx_bytes,
+                 int64_t n, int64_t m, double eps, double tau2, double tol, int64_t max_iter,
+                 void* workspace, int64_t workspace_bytes, float* out, float* sol_out,
+                 int64_t* iters_host, double* resid_host, void* stream) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(x && y && v && a && b && r_ptr && c_ptr && workspace && out,
+                   "hvp: null argument");
+  HvpArgs h;
+  h.x = x; h.y = y; h.v = v; h.a = a; h.b = b; h.d = d;
+  h.r_ptr = r_ptr; h.r_idx = r_idx; h.r_T = r_T;
+  h.c_ptr = c_ptr; h.c_idx = c_idx; h.c_T = c_T; h.idx_bytes = idx_bytes;
+  h.n = n; h.m = m; h.eps = eps; h.tau2 = tau2; h.tol = tol; h.max_iter = max_iter;
+  h.ws = workspace; h.ws_bytes = (size_t)workspace_bytes;
+  h.out = out; h.sol_out = sol_out; h.iters_host = iters_host; h.resid_host = resid_host;
+  return hvp(h, ST(stream));
 }
 
 int sinkslot_csr_workspace_bytes(int64_t nnz, int64_t nseg, int64_t* bytes_host) {

@@ -85,6 +85,9 @@ constexpr size_t kSmemCap = 227 * 1024;
 #ifndef SINKSLOT_TILE_PF_BYTES
 #define SINKSLOT_TILE_PF_BYTES (1 << 30)
 #endif
+#ifndef SINKSLOT_TILE_EARLY_INIT
+#define SINKSLOT_TILE_EARLY_INIT 1
+#endif
 constexpr int kStages = SINKSLOT_TILE_STAGES;
 constexpr int kPfLead = SINKSLOT_TILE_PF_LEAD;
 constexpr uint32_t kPfBytes = SINKSLOT_TILE_PF_BYTES;
@@ -166,9 +169,7 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
   g.smem_bytes = pipe_smem((int)R, 1 << logW);
   const int64_t ntiles = (int64_t)g.P * g.B;
-  // each tile: an odd number of slabs; then one group of slabs of tail padding,
-  // which a consumer warp's group loads may read past the last tile
-  g.cap = nnz + (2 * kSlab - 1) * ntiles + kGroup * kSlab;
+  g.cap = nnz + (2 * kSlab - 1) * ntiles;  // each tile: an odd number of slabs
   Carver cv(nullptr, 0);
   cv.take<int64_t>(8);            // header: [0] longest row of <= kMaxTiledRow entries
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
@@ -988,25 +989,12 @@ __device__ __forceinline__ void prefetch_entries(const uint2* ent, int64_t e0, i
 // Lane `lane` of slabs g .. g+kGroup-1 of the tile whose entries start at e0
 // (only the slabs below nsl are loaded): coalesced 8-byte streaming loads, 256
 // bytes per slab.
-#ifndef SINKSLOT_TILE_UNCOND_LOADS
-#define SINKSLOT_TILE_UNCOND_LOADS 0
-#endif
 __device__ __forceinline__ void load_group(const uint2* ent, int64_t e0, int nsl, int g, int lane,
                                            uint2 (&e)[kGroup]) {
   const uint2* p = ent + e0 + (int64_t)g * kSlab + lane;
-#if SINKSLOT_TILE_UNCOND_LOADS
-  // a group that starts inside the tile loads all its slabs: those past the
-  // tile's end (at most kGroup - 1) read the next tile or the layout's tail
-  // padding, a whole group long; process_group ignores them
-  if (g < nsl) {
-#pragma unroll
-    for (int j = 0; j < kGroup; ++j) e[j] = ld_stream(p + j * kSlab);
-  }
-#else
 #pragma unroll
   for (int j = 0; j < kGroup; ++j)
     if (g + j < nsl) e[j] = ld_stream(p + j * kSlab);
-#endif
 }
 
 // The terms of a group of `cnt` (>= 1) slabs; when the whole group exists one
@@ -1081,9 +1069,18 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  // The kernel may start while the previous launch of the loop is finishing
+  // (programmatic dependent launch).  Before chain_enter it touches only what
+  // no running launch writes: its shared memory, the layout, and (consumers,
+  // first panel) the row state's inputs base / self_old / the CSR offsets --
+  // self_old is this side's own output, written at least three launches back.
+  // The gathered potential, the stabilisers of a max pass, the error word and
+  // the other side's handed-back counter are read or written after it.
+#if !SINKSLOT_TILE_EARLY_INIT
   chain_enter();
   // a pipeline wait of an earlier launch timed out: do nothing (the host reports it)
   if (*(volatile int*)a.err != 0) return;
+#endif
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(pot_full(s), 1);
@@ -1092,12 +1089,18 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     *abort_w = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
+#if !SINKSLOT_TILE_EARLY_INIT
   if (a.fb_reset && blockIdx.x == 0 && tid == 0) *a.fb_reset = 0;
+#endif
   __syncthreads();
 
   if (warp == kConsumerWarps) {
     // ---------------- producer warp: lane 0 issues every copy ----------------
     if (lane != 0) return;
+#if SINKSLOT_TILE_EARLY_INIT
+    chain_enter();
+    if (*(volatile int*)a.err != 0) return;
+#endif
     long long nb = 0;  // blocks issued so far: stage nb % kStages, use nb / kStages
     int sb = 0;
     uint32_t ub = 0;   // parity of the current use of stage sb
@@ -1155,9 +1158,18 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   int sb = 0;
   uint32_t ub = 0;
   bool ok = true;
+  bool entered = !SINKSLOT_TILE_EARLY_INIT;
+  if (!entered && a.sigma != nullptr) {
+    chain_enter();  // the stabilisers are the previous launch's output
+    entered = true;
+    if (*(volatile int*)a.err != 0) ok = false;
+    if (a.fb_reset && blockIdx.x == 0 && tid == 0) *a.fb_reset = 0;
+  }
   // Control flow that crosses a consumer barrier follows the shared abort word
-  // (identical for all consumers after bar.sync), never a thread-local flag.
-  for (int p = blockIdx.x; !*abort_w && p < a.P; p += gridDim.x) {
+  // (identical for all consumers after bar.sync), never a thread-local flag --
+  // except the error word read right after chain_enter, which every thread
+  // reads after the previous launch has completed (the same value for all).
+  for (int p = blockIdx.x; ok && !*abort_w && p < a.P; p += gridDim.x) {
     const int64_t row0 = (int64_t)p * a.R;
     const int rows = (int)std::min<int64_t>(a.R, a.nseg - row0);
     if (rows <= 0) break;
@@ -1193,6 +1205,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     int64_t f1n = a.B > 1 ? a.tstart[pb + 2] : e1;
     uint2 en[kGroup];
     load_group(a.ent, e0, (int)((e1 - e0) / kSlab), kGroup * warp, lane, en);
+    if (!entered) {
+      chain_enter();
+      entered = true;
+      if (*(volatile int*)a.err != 0) break;
+      if (a.fb_reset && blockIdx.x == 0 && tid == 0) *a.fb_reset = 0;
+    }
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     for (int b = 0; ok && b < a.B; ++b) {
       const int nsl = (int)((e1 - e0) / kSlab);

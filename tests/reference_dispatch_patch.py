@@ -8,7 +8,9 @@ Three edits, each anchored on a line of the reference's dispatcher:
 2. the accepted backend names (``sinkslot_solve``'s first check) gain "b200";
 3. before the backend resolution (``if backend == "triton":`` inside
    ``sinkslot_solve``): "b200", or "auto" with the library present and X a CUDA
-   float32 tensor, returns ``sinkslot_b200.sinkslot_solve(...)``.
+   float32 tensor, returns ``sinkslot_b200.sinkslot_solve(...)``'s fields as
+   the reference's own ``SinkslotSolveResult`` (its return annotation is
+   checked at run time).
 """
 
 from __future__ import annotations
@@ -27,11 +29,11 @@ except Exception:
 
 DISPATCH_BLOCK = '''    if backend == "b200" or (backend == "auto" and _HAS_B200 and X.is_cuda
                              and X.dtype == torch.float32):
-        return _b200.sinkslot_solve(
+        return SinkslotSolveResult(*_b200.sinkslot_solve(
             X, Y, a, b, eps, L, seed, n_iters, stop_mode=stop_mode,
             stop_max_iter=stop_max_iter, stop_tol=stop_tol,
             stop_check_every=stop_check_every, chunk=chunk, variant=variant,
-            alpha=alpha)
+            alpha=alpha))
 '''
 
 

@@ -188,3 +188,25 @@ def test_batched_solves_equal_single_solves(cuda):
     assert all(r.converged for r in out)
     with pytest.raises(TypeError):
         sinkslot_solve_batched([(probs[0][0],)], eps=0.05)
+
+
+@pytest.mark.parametrize("case", ["small_nonuniform", "bench_shape", "cfg1", "unequal_ties",
+                                  "zero_weights"])
+def test_cost_bit_exact_vs_reference_cpu_run(cuda, oracle, case):
+    """sparse_sqeuclidean_cost (and the fused cost of cost_and_lam) on the device
+    against the reference's own CPU run of `(x[rows]-y[cols]).square().sum(1)`
+    (solver.py:346), stored as a sha256 in the golden fixture, on the support
+    of that run: bit for bit."""
+    import hashlib
+    from sinkslot_b200 import sparse_sqeuclidean_cost
+    from sinkslot_b200.solver import cost_and_lam
+    meta, g, (x, y, a, b) = _inputs(case, cuda)
+    rows, cols, S = oracle.sot_plan_coo(g["x"], g["y"], g["a"], g["b"], meta["L"], 0,
+                                        builder="cpu")
+    r, c = torch.from_numpy(rows).to(cuda), torch.from_numpy(cols).to(cuda)
+    cost = sparse_sqeuclidean_cost(x, y, r, c).cpu().numpy()
+    assert hashlib.sha256(np.ascontiguousarray(cost).tobytes()).hexdigest() == meta["sha_cost"]
+    np.testing.assert_array_equal(cost, oracle.sqeuclid_cost(g["x"], g["y"], rows, cols))
+    _, fused = cost_and_lam(x, y, r, c, torch.from_numpy(S).to(cuda), meta["eps"],
+                            want_cost=True)
+    np.testing.assert_array_equal(fused.cpu().numpy(), cost)
