@@ -114,6 +114,8 @@ def gmm_unit_cloud(n: int, k: int, d: int, std: float) -> torch.Tensor:
 #         torch.distributed.run the fixed problem is partitioned over the ranks
 #         (strong scaling)
 CONFIGS = {
+    "cfg1": dict(n=10000, m=10000, d=2, L=64, eps=0.05, n_iters=200, data_seed=0, shift=0.0,
+                 proj_seed=0, variant="alternating"),
     "cfg2": WORKLOAD,
     "cfg3": dict(n=1 << 21, m=1 << 20, d=3, L=128, eps=0.005, n_iters=20000, data_seed=4,
                  gen="gmm_unit", components=16, std=0.05, weights="dirichlet", proj_seed=0,
@@ -126,6 +128,9 @@ CONFIGS = {
                  variant="alternating"),
 }
 CONFIG_NAMES = {
+    "cfg1": "sinkslot CPU-runnable configuration, N=M=10^4, d=2, x,y~N(0,I) (seed 0), uniform "
+            "weights, eps=0.05, L=64, 200 alternating iterations; SamplesLoss cost, potentials, "
+            "slot_grad",
     "cfg3": "sinkslot colour-transfer shape, N=2^21 x M=2^20, d=3, 16-component mixtures in "
             "[0,1]^3, Dirichlet weights, L=128, eps=0.005, symmetric, marginal stop 1e-6/5 "
             "(seed 4); then plan + barycentric map",
@@ -563,11 +568,87 @@ def _base_line(cfg, w, value, unit, world, steps, warmup, ms_per_step, clocks, e
 
 
 METRICS = {
+    "cfg1": "Sinkhorn iter/s at N=M=10^4,d=2,L=64 fp32 (launch-bound small problem)",
     "cfg3": "colour-transfer-shaped solve: symmetric Sinkhorn iter/s at N=2^21,M=2^20,d=3,L=128 "
             "fp32 (marginal stop)",
     "cfg4": "gradient-flow outer steps/s at N=M=2^18,d=2,L=100 fp32 (support rebuilt per step)",
     "cfg5": "Sinkhorn iter/s at N=M=2^24,d=3,L=64 fp32, rows/cols partitioned over the GPUs",
 }
+
+
+def run_cfg1(args):
+    """The small configuration the reference runs on CPU: a step is one
+    iteration of the 200-iteration solve loop (launch-bound: ~8 MB of CSR/CSC,
+    L2-resident); e2e is SamplesLoss (cost, backward) + the potentials from host
+    tensors, per solve of 200 iterations."""
+    import sinkslot_b200
+    from sinkslot_b200 import SamplesLoss
+    from sinkslot_b200.sinkhorn_solvers import sinkslot_alternating_b200
+    from sinkslot_b200.solver import _to_csr, cost_and_lam, sot_plan_coo
+
+    world, rank, local = dist_setup(1)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sinkslot_b200.load_library()
+    w = CONFIGS["cfg1"]
+    n, m = w["n"], w["m"]
+    x, y, a, b = make_inputs(0, w)
+    X, Y, A, B = (t.to(dev) for t in (x, y, a, b))
+    stream = torch.cuda.current_stream(dev)
+
+    def setup():
+        rows, cols, S = sot_plan_coo(X, Y, A, B, L=w["L"], seed=w["proj_seed"])
+        lam, _ = cost_and_lam(X, Y, rows, cols, S, w["eps"])
+        r = _to_csr(rows, cols, lam, n, want_perm=False)
+        c = _to_csr(cols, rows, lam, m, want_perm=False)
+        return int(rows.numel()), (r[0], r[1], r[2], c[0], c[1], c[2], A.log(), B.log(), n, m)
+
+    setup()
+    (nnz, csr), setup_ms = _timed(stream, setup)
+    sinkslot_alternating_b200(*csr, max(args.warmup, 3))
+    K = max(1, min(args.steps, 2000))
+    sampler = ClockSampler(local)
+    sampler.start()
+    _, ms = _timed(stream, lambda: sinkslot_alternating_b200(*csr, K))
+    clocks = sampler.stop()
+    value = K / (ms / 1e3)
+    b_iter = _side_bytes(csr[1], nnz, n) + _side_bytes(csr[4], nnz, m)
+    peak, peak_kind = measured_peak_gbs()
+    loss_fn = SamplesLoss(eps=w["eps"], L=w["L"], seed=w["proj_seed"], n_iters=w["n_iters"])
+    xh, yh = x.pin_memory(), y.pin_memory()
+    gh = torch.empty_like(x).pin_memory()
+
+    def e2e():
+        Xd = xh.to(dev, non_blocking=True).requires_grad_(True)
+        Yd = yh.to(dev, non_blocking=True)
+        loss = loss_fn(Xd, Yd)
+        (g,) = torch.autograd.grad(loss, [Xd])
+        gh.copy_(g, non_blocking=True)
+
+    e2e()
+    reps = 20
+    _, e2e_ms = _timed(stream, lambda: [e2e() for _ in range(reps)])
+    tri = None if args.no_triton else triton_reference_leg(X, Y, A, B, w, K, value)
+    line = _base_line("cfg1", w, value, UNIT, 1, K, max(args.warmup, 3), ms / K, clocks, {
+        "nnz": nnz, "setup_ms": round(setup_ms, 2), "idx_bytes": csr[1].element_size(),
+        "l2": "L2-resident: %.1f MB of CSR+CSC per iteration" % (b_iter / 1e6),
+        "solve_us_per_iteration": round(ms / K * 1e3, 2)})
+    line["roofline"] = {"bound": "hbm", "achieved": round(b_iter * value / 1e9, 1), "peak": peak,
+                        "unit": "GB/s", "frac": round(b_iter * value / 1e9 / peak, 4),
+                        "peak_source": peak_kind, "traffic": None,
+                        "kernel": "exact half-step kernel (below the tiled pass's threshold); "
+                                  "launch-bound, data L2-resident"}
+    line["cpu_baseline"] = None
+    line["triton_reference"] = tri
+    line["e2e"] = {"value": round(reps * w["n_iters"] / (e2e_ms / 1e3), 2), "unit": UNIT,
+                   "h2d_bytes_per_step": (x.numel() + y.numel()) * 4,
+                   "d2h_bytes_per_step": x.numel() * 4,
+                   "step": "SamplesLoss forward (support build + 200 iterations + cost) and "
+                           "backward from pinned host x, y; the gradient back",
+                   "ms_per_solve": round(e2e_ms / reps, 3)}
+    line["gpu_launches"] = 2 * K
+    print(json.dumps(line), flush=True)
 
 
 def run_cfg3(args):
@@ -1001,9 +1082,10 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--config", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
-                    help="workload: cfg2 the headline (default); cfg3 colour-transfer shape; "
-                         "cfg4 gradient flow; cfg5 N=M=2^24 (strong scaling under torchrun)")
+    ap.add_argument("--config", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
+                    help="workload: cfg2 the headline (default); cfg1 N=M=10^4 (small, "
+                         "launch-bound); cfg3 colour-transfer shape; cfg4 gradient flow; cfg5 "
+                         "N=M=2^24 (strong scaling under torchrun)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-triton", action="store_true",
                     help="skip timing the reference's Triton kernel on the same device")
@@ -1024,6 +1106,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "cfg1":
+        run_cfg1(args)
     elif args.config == "cfg3":
         run_cfg3(args)
     elif args.config == "cfg4":

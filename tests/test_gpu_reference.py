@@ -224,8 +224,8 @@ def test_cost_and_lam_match_reference_on_the_device(cuda, ref):
     the device, and lam against its expression (sinkhorn_solvers.py:700) there.
     The cost kernel sums the d squared differences in index order, as the
     reference's CPU run does (bit for bit, test_gpu_api.py); torch's CUDA
-    reduction may associate the three terms differently, so on the device the
-    bar is one rounding of the sum."""
+    reduction associates three terms as (t0 + t2) + t1 (measured on B200), so on
+    the device the two differ by at most two units in the last place."""
     from sinkslot_b200 import sparse_sqeuclidean_cost
     from sinkslot_b200.solver import cost_and_lam
     from sinkslot import solver as rs
@@ -234,11 +234,11 @@ def test_cost_and_lam_match_reference_on_the_device(cuda, ref):
     rows, cols, S = rs.sot_plan_coo(X, Y, A, B, L=32, seed=0, ot1d=rs._ot_1d_coo_batched_cuda)
     want = rs.sparse_sqeuclidean_cost(X, Y, rows, cols, use_triton=False)
     got = sparse_sqeuclidean_cost(X, Y, rows, cols)
-    torch.testing.assert_close(got, want, rtol=2 ** -23, atol=0)
+    torch.testing.assert_close(got, want, rtol=3e-7, atol=0)
     lam, cost = cost_and_lam(X, Y, rows, cols, S, 0.01, want_cost=True)
     assert torch.equal(cost, got)
     lam_ref = S.clamp_min(torch.finfo(S.dtype).tiny).log() - want / 0.01
-    torch.testing.assert_close(lam, lam_ref, rtol=5e-7, atol=0)
+    torch.testing.assert_close(lam, lam_ref, rtol=1e-6, atol=0)
 
 
 def test_plan_gradient_and_loss_match_reference(cuda, ref):
