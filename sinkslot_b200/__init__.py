@@ -6,6 +6,7 @@ backed by ``libsinkslot_b200.so`` (C ABI: ``include/sinkslot_b200.h``).
 Inputs must be float32 CUDA tensors; there is no CPU or library fallback.
 """
 
+from . import ops as _ops  # noqa: F401  (registers torch.ops.sinkslot_b200.*)
 from .solver import (
     get_random_projections,
     sot_plan_coo,

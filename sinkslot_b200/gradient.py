@@ -19,6 +19,13 @@ from .sinkhorn_solvers import plan_values, sinkslot_solve
 
 
 def _bary(T_vals, rows, cols, x, y, a=None, want_tx=True, want_ty=True, want_grad=False):
+    Tx, Ty, g = torch.ops.sinkslot_b200.barycentric(T_vals, rows, cols, x, y, a, bool(want_tx),
+                                                     bool(want_ty), bool(want_grad))
+    return (Tx if want_tx else None), (Ty if want_ty else None), (g if want_grad else None)
+
+
+def _bary_impl(T_vals, rows, cols, x, y, a, want_tx, want_ty, want_grad):
+    """The body of the ``sinkslot_b200::barycentric`` operator."""
     dev = x.device
     n, d = x.shape
     m = y.shape[0]

@@ -52,6 +52,20 @@ def hvp_x_sqeuclid_from_potentials(X, Y, a, v, rows, cols, T_vals, eps, *, tau2=
         if not t.is_cuda or t.dtype != torch.float32:
             raise ValueError(f"hvp: {name} must be a float32 CUDA tensor (got {t.dtype} on "
                              f"{t.device}); sinkslot_b200 has no CPU path")
+    out, info = torch.ops.sinkslot_b200.hvp_from_potentials(
+        X, Y, a, v, rows, cols, T_vals, float(eps), float(tau2), float(solve_tol),
+        int(max_cg_iter))
+    if return_info:
+        it, res = info.tolist()
+        return out, HvpInfo(int(it), float(res))
+    return out
+
+
+def _hvp_impl(X, Y, a, v, rows, cols, T_vals, eps, tau2, solve_tol, max_cg_iter):
+    """The body of the ``sinkslot_b200::hvp_from_potentials`` operator:
+    (H v, iterations, relative residual)."""
+    n, d = X.shape
+    m = Y.shape[0]
     dev = X.device
     X, Y, a, v = X.contiguous(), Y.contiguous(), a.contiguous(), v.contiguous()
     rows = rows.to(torch.int64).contiguous()
@@ -71,9 +85,7 @@ def hvp_x_sqeuclid_from_potentials(X, Y, a, v, rows, cols, T_vals, eps, *, tau2=
              ptr(r_T), ptr(c_ptr), ptr(c_idx), ptr(c_T), _idx_bytes(r_idx), n, m, float(eps),
              float(tau2), float(solve_tol), int(max_cg_iter), ptr(ws), ws.numel(), ptr(out), None,
              ctypes.byref(iters), ctypes.byref(resid), stream_of(dev))
-    if return_info:
-        return out, HvpInfo(int(iters.value), float(resid.value))
-    return out
+    return out, int(iters.value), float(resid.value)
 
 
 @jaxtyped(typechecker=beartype)

@@ -49,13 +49,17 @@ def seg_lse_online(indptr, colidx, lam, phi, psi, n, block=None, num_warps=None,
     (``LSE`` itself when ``base`` is None), written into ``out`` when given
     (reference: sinkhorn_solvers.py:121-146).  ``block``/``num_warps`` are
     accepted for compatibility."""
-    dev = lam.device
     if out is None:
-        out = torch.empty(n, dtype=lam.dtype, device=dev)
+        return torch.ops.sinkslot_b200.seg_lse(indptr, colidx, lam, phi, psi, int(n), base)
+    _seg_lse_impl(indptr, colidx, lam, phi, psi, n, base, out)
+    return out
+
+
+def _seg_lse_impl(indptr, colidx, lam, phi, psi, n, base, out):
+    dev = lam.device
     with torch.cuda.device(dev):
         call("sinkslot_seg_lse", ptr(indptr), ptr(colidx), _idx_bytes(colidx), ptr(lam),
              colidx.numel(), ptr(phi), ptr(psi), ptr(base), n, ptr(out), stream_of(dev))
-    return out
 
 
 class SinkslotSolveResult(NamedTuple):
@@ -253,7 +257,23 @@ def sinkslot_solve(X: Float[torch.Tensor, "n d"], Y: Float[torch.Tensor, "m d"],
     stop = None if stop_mode == "fixed" else SimpleNamespace(
         mode=stop_mode, max_iter=stop_max_iter, tol=stop_tol, check_every=stop_check_every)
     _resolve_stop_mode(stop)
+    if stop_mode == "potential" and eps is None:
+        raise ValueError("eps is required for stop.mode == 'potential'")
+    phi, psi, rows, cols, S, info = torch.ops.sinkslot_b200.solve(
+        X, Y, a, b, float(eps), int(L), int(seed), int(n_iters), str(stop_mode),
+        int(stop_max_iter), float(stop_tol), int(stop_check_every),
+        None if chunk is None else int(chunk), str(variant), float(alpha))
+    it, conv, viol = info.tolist()
+    if stop_mode == "fixed":
+        return SinkslotSolveResult(phi, psi, rows, cols, S, int(it), None, None)
+    return SinkslotSolveResult(phi, psi, rows, cols, S, int(it), bool(conv), float(viol))
 
+
+def _solve_impl(X, Y, a, b, eps, L, seed, n_iters, stop_mode, stop_max_iter, stop_tol,
+                stop_check_every, chunk, variant, alpha):
+    """The body of the ``sinkslot_b200::solve`` operator (arguments validated)."""
+    stop = None if stop_mode == "fixed" else SimpleNamespace(
+        mode=stop_mode, max_iter=stop_max_iter, tol=stop_tol, check_every=stop_check_every)
     n, m = X.shape[0], Y.shape[0]
     rows, cols, S = sot_plan_coo(X, Y, a, b, L=L, seed=seed, chunk=chunk)
     lam, _ = cost_and_lam(X, Y, rows, cols, S, eps)
@@ -271,13 +291,18 @@ def sinkslot_solve(X: Float[torch.Tensor, "n d"], Y: Float[torch.Tensor, "m d"],
         phi, psi, it, converged, viol = sinkslot_alternating_b200(
             r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, n, m, n_iters, stop, eps,
             tiles=tiles)
-    return SinkslotSolveResult(phi, psi, rows, cols, S, it, converged, viol)
+    return phi, psi, rows, cols, S, it, converged, viol
 
 
 def plan_values(phi, psi, rows, cols, S, x, y, eps, grad_form: bool = False) -> torch.Tensor:
     """exp(phi[r] + psi[c] + log S - cost/eps) with the cost recomputed in-kernel.
     ``grad_form`` selects slot_grad's association (gradient.py:94-97) over
     sparse_transport_plan's (sinkhorn_solvers.py:757-758)."""
+    return torch.ops.sinkslot_b200.plan_values(phi, psi, rows, cols, S, x, y, float(eps),
+                                               bool(grad_form))
+
+
+def _plan_values_impl(phi, psi, rows, cols, S, x, y, eps, grad_form):
     dev = phi.device
     out = torch.empty(rows.numel(), dtype=torch.float32, device=dev)
     x, y = x.contiguous(), y.contiguous()

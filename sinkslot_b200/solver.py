@@ -139,7 +139,16 @@ def sot_plan_coo(
     if ot1d is not None and ot1d is not _ot_1d_coo_batched_cuda:
         raise ValueError("sot_plan_coo: sinkslot_b200 builds the support with the CUDA "
                          "builder's semantics only (ot1d must be None)")
-    dev = _require_cuda_f32("sot_plan_coo", X, Y, a, b)
+    _require_cuda_f32("sot_plan_coo", X, Y, a, b)
+    if chunk is not None and int(chunk) < 1:
+        raise ValueError("chunk must be a positive int")
+    return torch.ops.sinkslot_b200.sot_plan_coo(X, Y, a, b, int(L), int(seed),
+                                                None if chunk is None else int(chunk))
+
+
+def _sot_plan_coo_impl(X, Y, a, b, L: int, seed: int, chunk):
+    """The body of the ``sinkslot_b200::sot_plan_coo`` operator."""
+    dev = X.device
     n, d = X.shape
     m = Y.shape[0]
     thetas = torch.as_tensor(get_random_projections(d, L, seed), dtype=X.dtype, device=dev)
@@ -246,7 +255,8 @@ def sparse_sqeuclidean_cost(
     """``||x[rows] - y[cols]||^2`` per support entry (reference: solver.py:302-360).
 
     Computed by the fused sm_100a kernel with each operation rounded as the
-    reference's torch expression ``(x[rows]-y[cols]).square().sum(1)`` rounds it.
+    reference's torch expression ``(x[rows]-y[cols]).square().sum(1)`` rounds it
+    on the CPU (the d terms summed in index order).
     float32-only, like the reference's fused path; ``block`` and ``use_triton``
     are accepted for signature compatibility.
     """
@@ -254,7 +264,13 @@ def sparse_sqeuclidean_cost(
         raise ValueError(
             f"sparse_sqeuclidean_cost's fused path is float32-only (fixed float32 "
             f"accumulator); got x.dtype={x.dtype}, y.dtype={y.dtype}. Cast to float32 first.")
-    dev = _require_cuda_f32("sparse_sqeuclidean_cost", x, y)
+    _require_cuda_f32("sparse_sqeuclidean_cost", x, y)
+    return torch.ops.sinkslot_b200.sparse_sqeuclidean_cost(x, y, rows, cols)
+
+
+def _sqeuclid_cost_impl(x, y, rows, cols):
+    """The body of the ``sinkslot_b200::sparse_sqeuclidean_cost`` operator."""
+    dev = x.device
     x, y = x.contiguous(), y.contiguous()
     rows = rows.to(torch.int64).contiguous()
     cols = cols.to(torch.int64).contiguous()
