@@ -963,18 +963,6 @@ __device__ __forceinline__ void accumulate(uint32_t* st, float d) {
   atomicAdd(st + 2, (uint32_t)q & ((1u << kLoBits) - 1u));
 }
 
-#ifndef SINKSLOT_TILE_FLOAT_SUM
-#define SINKSLOT_TILE_FLOAT_SUM 0
-#endif
-// Float accumulation (SINKSLOT_TILE_FLOAT_SUM): each term exp(d) is added to the
-// row's fp32 sum with a shared-memory float atomic -- one atomic per entry, no
-// fixed-point conversion, no cap (a float sum holds any term below e^88; an
-// infinite, zero or NaN sum hands the row back) -- at the price of a summation
-// order that varies run to run (last-bit differences).
-__device__ __forceinline__ void accumulate_float(uint32_t* st, float d) {
-  atomicAdd(reinterpret_cast<float*>(st + 1), exp2_approx(d * 1.44269504088896341f));
-}
-
 __device__ __forceinline__ void flag_row(uint32_t* flags, uint2 e) {
   const uint32_t r = e.x >> 16;
   atomicOr(flags + (r >> 5), 1u << (r & 31));
@@ -1014,19 +1002,6 @@ __device__ __forceinline__ void load_group(const uint2* ent, int64_t e0, int nsl
 __device__ __forceinline__ void process_group(unsigned char* smem, uint32_t* flags,
                                               const float* cur, const uint2 (&e)[kGroup], int cnt,
                                               float capd) {
-#if SINKSLOT_TILE_FLOAT_SUM
-  (void)flags;
-  (void)capd;
-#pragma unroll
-  for (int j = 0; j < kGroup; ++j) {
-    if (j < cnt) {
-      uint32_t* st;
-      const float d = entry_exponent(smem, cur, e[j], st);
-      accumulate_float(st, d);
-    }
-  }
-  return;
-#endif
   if (cnt >= kGroup) {
     uint32_t* st[kGroup];
     float d[kGroup];
@@ -1276,14 +1251,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
         a.out[seg] = st[1] ? radix_to_float(st[1]) : -INFINITY;
         continue;
       }
-#if SINKSLOT_TILE_FLOAT_SUM
-      const float tot = __uint_as_float(st[1]);
-      const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;  // rows longer than kMaxTiledRow
-      if (flagged || !(tot > 0.0f) || tot == INFINITY) {
-        a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
-        continue;
-      }
-#else
       const unsigned long long q = ((unsigned long long)st[1] << kLoBits) + st[2];
       const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
       if (flagged || q < kFixMin) {
@@ -1291,7 +1258,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
         continue;
       }
       const float tot = (float)((double)q * kFixInv);
-#endif
       const float lse = __fadd_rn(__uint_as_float(st[0]), logf(tot));
       segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
                                  chk_bits, a.peers);
