@@ -11,8 +11,9 @@
 // Layout (built once per solve from the CSR side): tile (p, b) = the entries of
 // panel p whose column lies in block b, padded to a multiple of 32 entries (one
 // warp slab) and arranged so that a slab's rows fall in different shared-memory
-// banks (see tilekey_kernel); per entry one uint2 {row within the panel << 16 |
-// column within the block, fp32 lam bits}.  Padding names row R (a dummy row
+// banks (see tilekey_kernel); per entry one uint2 {meta, fp32 lam bits}, meta
+// holding the byte offsets of the row's state (row within the panel, times 4)
+// and of the column's potential (column within the block, times 4).  Padding names row R (a dummy row
 // of the panel state) with lam = -inf, so it adds an exact zero and the inner
 // loop needs no test for it.
 //
@@ -64,17 +65,12 @@ constexpr size_t kSmemCap = 227 * 1024;
 
 // Build-time tuning of the pipeline (defaults measured on B200):
 //   SINKSLOT_TILE_STAGES   depth of the potential-block ring
-//   SINKSLOT_TILE_ROWS_KB  budget for the per-row state; more panels than SMs
-//                          are used (each SM walks several) to stay within it
 //   SINKSLOT_TILE_MAX_LOGW widest potential block (2^x floats)
 //   SINKSLOT_TILE_PF_LEAD  tiles between the one whose entries the producer
 //                          prefetches into L2 and the one whose block it copies
 //   SINKSLOT_TILE_PF_BYTES largest single L2 prefetch (a tile's range is split)
 #ifndef SINKSLOT_TILE_STAGES
 #define SINKSLOT_TILE_STAGES 2
-#endif
-#ifndef SINKSLOT_TILE_ROWS_KB
-#define SINKSLOT_TILE_ROWS_KB 96
 #endif
 #ifndef SINKSLOT_TILE_MAX_LOGW
 #define SINKSLOT_TILE_MAX_LOGW 14
@@ -118,17 +114,38 @@ __host__ __device__ inline int64_t tile_slabs(int64_t n) {
 #endif
 constexpr int kGroup = SINKSLOT_TILE_GROUP;
 
-// Shared memory of the per-row state: rows 0..R-1 of the panel and a dummy row R
-// (the target of tile padding), 12 bytes each at offset 12 r: sigma (float),
-// high sum, low sum (uint32); then one flag bit per row.
-__host__ __device__ inline size_t rows_flags_off(int R) { return align_up((size_t)(R + 1) * 12, 16); }
-__host__ __device__ inline size_t rows_smem(int R) {
-  return align_up(rows_flags_off(R) + (size_t)((R + 1 + 31) / 32) * 4, 128);
-}
+// Shared memory of the tiled kernel, at fixed offsets (every address in the
+// inner loop is a register plus a constant):
+//   [0, kRingBytes)          kStages potential blocks of up to 2^kMaxLogW floats
+//   kSigOff + 4 r            sigma of panel row r (float)
+//   kHiOff + 4 r, kLoOff + 4 r  its high and low fixed-point sums (uint32)
+//   kFlagOff                 one flag bit per row, then the mbarriers
+// for rows r = 0 .. kRowCap - 1: the panel's R rows and the dummy row R (the
+// target of tile padding).
+constexpr int kMaxLogW = SINKSLOT_TILE_MAX_LOGW;
+static_assert(kMaxLogW >= 8 && kMaxLogW <= 14, "columns are stored as 16-bit byte offsets");
+constexpr uint32_t kStageBytes = 4u << kMaxLogW;
+constexpr uint32_t kRingBytes = (uint32_t)kStages * kStageBytes;
+// rows: 12 bytes of state and one flag bit each, in what the ring leaves
+constexpr uint32_t kRowCap =
+    (uint32_t)((kSmemCap - kRingBytes - kBarBytes - 256) * 8 / 97) & ~31u;
+static_assert(kRowCap >= 64 && kRowCap <= 16384, "row state: rows are 16-bit byte offsets");
+constexpr uint32_t kSigOff = kRingBytes;
+constexpr uint32_t kHiOff = kSigOff + 4 * kRowCap;
+constexpr uint32_t kLoOff = kHiOff + 4 * kRowCap;
+constexpr uint32_t kFlagOff = kLoOff + 4 * kRowCap;
+constexpr uint32_t kBarOff = (uint32_t)align_up(kFlagOff + kRowCap / 8, 128);
+constexpr size_t kTileSmem = kBarOff + kBarBytes;
+static_assert(kTileSmem <= kSmemCap, "tiled kernel shared memory");
 
-static size_t pipe_smem(int R, int W) {
-  return rows_smem(R) + (size_t)kStages * (size_t)W * 4 + kBarBytes;
+// Entry meta word: (row within the panel) * 4 << 16 | (column within the
+// block) * 4 -- the byte offsets of the row's state words and of the column's
+// potential in their shared-memory arrays.
+__host__ __device__ inline uint32_t entry_meta(uint32_t row, uint32_t col) {
+  return (row << 18) | (col << 2);
 }
+__host__ __device__ inline uint32_t meta_row(uint32_t x) { return x >> 18; }
+__host__ __device__ inline uint32_t meta_col(uint32_t x) { return (x & 0xFFFFu) >> 2; }
 
 // The direct builder cuts each panel into S sub-panels of Rs consecutive rows,
 // one CTA each, which keeps in shared memory two counters per (bank, block),
@@ -151,23 +168,19 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
   int64_t P = sms;
   if (nseg < P * 32) P = std::max<int64_t>(1, ceil_div64(nseg, 32));
   int64_t R = ceil_div64(nseg, P);
-  // per-row state within its budget (more panels per SM), R < 2^16, and room
-  // for the smallest rings
-  const size_t rows_budget = (size_t)SINKSLOT_TILE_ROWS_KB * 1024;
-  while ((rows_smem((int)std::min<int64_t>(R, 1 << 20)) > rows_budget && R > 32) || R > 65535 ||
-         pipe_smem((int)std::min<int64_t>(R, 1 << 20), 256) > kSmemCap) {
+  // the panel's rows and the dummy row within the row state (more panels per SM)
+  while (R + 1 > (int64_t)kRowCap) {
     P += sms;
     R = ceil_div64(nseg, P);
   }
-  // the widest block (fewest tiles) whose ring fits
+  // the widest block (fewest tiles), up to a ring stage
   int logW = 2;
-  while (logW < SINKSLOT_TILE_MAX_LOGW && ((int64_t)1 << logW) < m_o) ++logW;
-  while (logW > 8 && pipe_smem((int)R, 1 << logW) > kSmemCap) --logW;
+  while (logW < kMaxLogW && ((int64_t)1 << logW) < m_o) ++logW;
   g.P = (int)P;
   g.R = (int)R;
   g.logW = logW;
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
-  g.smem_bytes = pipe_smem((int)R, 1 << logW);
+  g.smem_bytes = kTileSmem;
   const int64_t ntiles = (int64_t)g.P * g.B;
   g.cap = nnz + (2 * kSlab - 1) * ntiles;  // each tile: an odd number of slabs
   Carver cv(nullptr, 0);
@@ -290,7 +303,7 @@ __global__ void tile_counts_kernel(const uint32_t* __restrict__ skey, int64_t nn
 
 // padding entries: the dummy row R, column 0, lam = -inf (a zero term)
 __global__ void fill_pad_kernel(uint2* __restrict__ ent, int64_t cap, int R) {
-  const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
+  const uint2 pad = make_uint2(entry_meta((uint32_t)R, 0u), __float_as_uint(-INFINITY));
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < cap;
        q += (int64_t)gridDim.x * blockDim.x)
     ent[q] = pad;
@@ -318,7 +331,7 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
     const int64_t pos = ts + ((int64_t)(p - lane * ns) << 5) + lane;
     const uint32_t r = rowid[k];
     const uint32_t c = (uint32_t)idx[k];
-    ent[pos] = make_uint2(((r % (uint32_t)R) << 16) | (c & wmask), __float_as_uint(lam[k]));
+    ent[pos] = make_uint2(entry_meta(r % (uint32_t)R, c & wmask), __float_as_uint(lam[k]));
   }
 }
 
@@ -484,7 +497,7 @@ __global__ void __launch_bounds__(kBuildThreads, 1) panel_scatter_kernel(
     d.tmp[i] = all;
   }
   __syncthreads();
-  const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
+  const uint2 pad = make_uint2(entry_meta((uint32_t)R, 0u), __float_as_uint(-INFINITY));
   for (int b = tid; b < B; b += kBuildThreads) {
     // each bank's first sorted position in the tile; padding after the entries
     uint32_t run = 0;
@@ -538,7 +551,7 @@ __global__ void __launch_bounds__(kBuildThreads, 1) panel_scatter_kernel(
       const uint32_t ns = (uint32_t)((d.ts[b + 1] - t0) >> 5);
       const uint32_t ln = qq / ns;
       ent[t0 + ((int64_t)(qq - ln * ns) << 5) + ln] =
-          make_uint2(((uint32_t)cur.r << 16) | (c & wmask), __float_as_uint(l_cur));
+          make_uint2(entry_meta((uint32_t)cur.r, c & wmask), __float_as_uint(l_cur));
     }
     cur = nxt;
     c_cur = c_n;
@@ -550,7 +563,7 @@ __global__ void __launch_bounds__(kBuildThreads, 1) panel_scatter_kernel(
 // padding entries after the last tile: [*end, cap)
 __global__ void fill_tail_kernel(uint2* __restrict__ ent, const int64_t* __restrict__ end,
                                  int64_t cap, int R) {
-  const uint2 pad = make_uint2((uint32_t)R << 16, __float_as_uint(-INFINITY));
+  const uint2 pad = make_uint2(entry_meta((uint32_t)R, 0u), __float_as_uint(-INFINITY));
   for (int64_t q = *end + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < cap;
        q += (int64_t)gridDim.x * blockDim.x)
     ent[q] = pad;
@@ -655,7 +668,7 @@ __global__ void __launch_bounds__(kPlaceThreads, 2) tile_colbank_kernel(
     // entries per (row bank, column class), padding excluded
     for (uint32_t q = tid; q < (uint32_t)len; q += kPlaceThreads) {
       const uint32_t x = tbuf[q].x;
-      if ((x >> 16) < (uint32_t)R) atomicAdd(&ecnt[(x >> 16) & (kBanks - 1)][x & 31u], 1u);
+      if (meta_row(x) < (uint32_t)R) atomicAdd(&ecnt[meta_row(x) & (kBanks - 1)][meta_col(x) & 31u], 1u);
     }
     __syncthreads();
     if (warp == 0) {
@@ -700,7 +713,7 @@ __global__ void __launch_bounds__(kPlaceThreads, 2) tile_colbank_kernel(
         const uint32_t j = j0 + lane;
         const bool v = j < c;
         const uint2 e = v ? tbuf[S + j] : make_uint2(0u, 0u);
-        const uint32_t cls = v ? (e.x & 31u) : 32u;
+        const uint32_t cls = v ? (meta_col(e.x) & 31u) : 32u;
         const uint32_t peers = __match_any_sync(0xffffffffu, cls);
         const uint32_t base = v ? run_k[rw][cls] : 0u;
         __syncwarp();
@@ -931,19 +944,28 @@ struct TKArgs {
   unsigned int* done;
 };
 
-// State of panel row r: {sigma bits, high sum, low sum} at byte 12 r of the
-// dynamic shared memory (a fixed base, so the address is one multiply).
-__device__ __forceinline__ uint32_t* row_state(unsigned char* smem, uint32_t r) {
-  return reinterpret_cast<uint32_t*>(smem + r * 12u);
+// The state words of panel row r, addressed by its byte offset 4 r (the high
+// half of an entry's meta word): sigma, high sum and low sum, in three arrays
+// at fixed offsets.
+__device__ __forceinline__ float* row_sigma(unsigned char* smem, uint32_t roff) {
+  return reinterpret_cast<float*>(smem + kSigOff + roff);
+}
+__device__ __forceinline__ uint32_t* row_hi(unsigned char* smem, uint32_t roff) {
+  return reinterpret_cast<uint32_t*>(smem + kHiOff + roff);
+}
+__device__ __forceinline__ uint32_t* row_lo(unsigned char* smem, uint32_t roff) {
+  return reinterpret_cast<uint32_t*>(smem + kLoOff + roff);
 }
 
-// One entry {row << 16 | column, lam bits}: the exponent d = lam + cur[column]
-// - sigma of its term, and the state of its row.  Padding entries name the
-// dummy row with lam = -inf, so d = -inf and the term is an exact zero.
-__device__ __forceinline__ float entry_exponent(unsigned char* smem, const float* cur, uint2 e,
-                                                uint32_t*& st) {
-  st = row_state(smem, e.x >> 16);
-  return __fsub_rn(__fadd_rn(__uint_as_float(e.y), cur[e.x & 0xFFFFu]), __uint_as_float(st[0]));
+// One entry {meta, lam bits} against ring stage S: the exponent d = lam +
+// potential[column] - sigma of its term, and its row's byte offset.  Padding
+// entries name the dummy row with lam = -inf, so d = -inf and the term is an
+// exact zero.
+template <int S>
+__device__ __forceinline__ float entry_exponent(unsigned char* smem, uint2 e, uint32_t& roff) {
+  roff = e.x >> 16;
+  const float pot = *reinterpret_cast<const float*>(smem + S * kStageBytes + (e.x & 0xFFFFu));
+  return __fsub_rn(__fadd_rn(__uint_as_float(e.y), pot), *row_sigma(smem, roff));
 }
 
 // 2^x (hardware approximation; results below 2^-126 flush to zero, far below
@@ -957,14 +979,14 @@ __device__ __forceinline__ float exp2_approx(float x) {
 // exp(d) in 2^-32 fixed point, added to the row's high and low partial sums.
 // Called for every entry; when d exceeds the cap (or is NaN) the caller has
 // flagged the row for the exact pass and its sums are unused.
-__device__ __forceinline__ void accumulate(uint32_t* st, float d) {
+__device__ __forceinline__ void accumulate(unsigned char* smem, uint32_t roff, float d) {
   const unsigned long long q = __float2ull_rn(exp2_approx(d * 1.44269504088896341f) * kFixScale);
-  atomicAdd(st + 1, (uint32_t)(q >> kLoBits));
-  atomicAdd(st + 2, (uint32_t)q & ((1u << kLoBits) - 1u));
+  atomicAdd(row_hi(smem, roff), (uint32_t)(q >> kLoBits));
+  atomicAdd(row_lo(smem, roff), (uint32_t)q & ((1u << kLoBits) - 1u));
 }
 
 __device__ __forceinline__ void flag_row(uint32_t* flags, uint2 e) {
-  const uint32_t r = e.x >> 16;
+  const uint32_t r = meta_row(e.x);
   atomicOr(flags + (r >> 5), 1u << (r & 31));
 }
 
@@ -997,18 +1019,18 @@ __device__ __forceinline__ void load_group(const uint2* ent, int64_t e0, int nsl
     if (g + j < nsl) e[j] = ld_stream(p + j * kSlab);
 }
 
-// The terms of a group of `cnt` (>= 1) slabs; when the whole group exists one
-// vote checks the cap of its terms.
+// The terms of a group of `cnt` (>= 1) slabs against ring stage S; when the
+// whole group exists one vote checks the cap of its terms.
+template <int S>
 __device__ __forceinline__ void process_group(unsigned char* smem, uint32_t* flags,
-                                              const float* cur, const uint2 (&e)[kGroup], int cnt,
-                                              float capd) {
+                                              const uint2 (&e)[kGroup], int cnt, float capd) {
   if (cnt >= kGroup) {
-    uint32_t* st[kGroup];
+    uint32_t ro[kGroup];
     float d[kGroup];
     bool in_cap = true;
 #pragma unroll
     for (int j = 0; j < kGroup; ++j) {
-      d[j] = entry_exponent(smem, cur, e[j], st[j]);
+      d[j] = entry_exponent<S>(smem, e[j], ro[j]);
       in_cap &= d[j] <= capd;
     }
     if (!__all_sync(0xffffffffu, in_cap)) {
@@ -1017,31 +1039,33 @@ __device__ __forceinline__ void process_group(unsigned char* smem, uint32_t* fla
         if (!(d[j] <= capd)) flag_row(flags, e[j]);
     }
 #pragma unroll
-    for (int j = 0; j < kGroup; ++j) accumulate(st[j], d[j]);
+    for (int j = 0; j < kGroup; ++j) accumulate(smem, ro[j], d[j]);
   } else {
 #pragma unroll
     for (int j = 0; j < kGroup - 1; ++j) {
       if (j < cnt) {
-        uint32_t* st;
-        const float d = entry_exponent(smem, cur, e[j], st);
+        uint32_t ro;
+        const float d = entry_exponent<S>(smem, e[j], ro);
         if (!(d <= capd)) flag_row(flags, e[j]);
-        accumulate(st, d);
+        accumulate(smem, ro, d);
       }
     }
   }
 }
 
-// Max mode: the largest term lam + cur[column] of each row, as the
+// Max mode: the largest term lam + potential[column] of each row, as the
 // order-preserving integer image of the float (float_to_radix) in the row's
-// first sum word, which starts at 0 (below the image of every float).
-// Padding adds -inf to the dummy row.
-__device__ __forceinline__ void process_group_max(unsigned char* smem, const float* cur,
-                                                  const uint2 (&e)[kGroup], int cnt) {
+// high-sum word, which starts at 0 (below the image of every float).  Padding
+// adds -inf to the dummy row.
+template <int S>
+__device__ __forceinline__ void process_group_max(unsigned char* smem, const uint2 (&e)[kGroup],
+                                                  int cnt) {
 #pragma unroll
   for (int j = 0; j < kGroup; ++j) {
     if (j < cnt) {
-      uint32_t* st = row_state(smem, e[j].x >> 16);
-      atomicMax(st + 1, float_to_radix(__fadd_rn(__uint_as_float(e[j].y), cur[e[j].x & 0xFFFFu])));
+      const float pot =
+          *reinterpret_cast<const float*>(smem + S * kStageBytes + (e[j].x & 0xFFFFu));
+      atomicMax(row_hi(smem, e[j].x >> 16), float_to_radix(__fadd_rn(__uint_as_float(e[j].y), pot)));
     }
   }
 }
@@ -1050,17 +1074,55 @@ __device__ __forceinline__ float radix_to_float(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
+// A consumer warp's groups of one tile -- slabs [0, nsl) of the entries from
+// e0 -- against ring stage S.  Each group is loaded one ahead (in `en`): behind
+// the warp's last group of this tile its first group of the next tile (f0,
+// nsl_next) goes in flight.
+template <int S, int OUT>
+__device__ __forceinline__ void consume_tile(unsigned char* smem, uint32_t* flags,
+                                             const uint2* ent, int64_t e0, int nsl, int64_t f0,
+                                             int nsl_next, int warp, int lane, float capd,
+                                             uint2 (&en)[kGroup]) {
+  constexpr int kStep = kGroup * kConsumerWarps;
+  for (int g = kGroup * warp; g < nsl; g += kStep) {
+    uint2 e[kGroup];
+#pragma unroll
+    for (int j = 0; j < kGroup; ++j) e[j] = en[j];
+    if (g + kStep < nsl)
+      load_group(ent, e0, nsl, g + kStep, lane, en);
+    else
+      load_group(ent, f0, nsl_next, kGroup * warp, lane, en);
+    if (OUT == kOutMax)
+      process_group_max<S>(smem, e, nsl - g);
+    else
+      process_group<S>(smem, flags, e, nsl - g, capd);
+  }
+}
+
+// consume_tile with the stage index s (< kStages) as a template argument, so
+// that the potential's address is the meta word's low half plus a constant
+template <int OUT, int S = 0>
+__device__ __forceinline__ void consume_stage(int s, unsigned char* smem, uint32_t* flags,
+                                              const uint2* ent, int64_t e0, int nsl, int64_t f0,
+                                              int nsl_next, int warp, int lane, float capd,
+                                              uint2 (&en)[kGroup]) {
+  if constexpr (S + 1 < kStages) {
+    if (s != S) {
+      consume_stage<OUT, S + 1>(s, smem, flags, ent, e0, nsl, f0, nsl_next, warp, lane, capd, en);
+      return;
+    }
+  }
+  consume_tile<S, OUT>(smem, flags, ent, e0, nsl, f0, nsl_next, warp, lane, capd, en);
+}
+
 template <int OUT, int CHK>
 __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const TKArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int W = 1 << a.logW;
-  // row state at offset 0 (12 bytes per row: sigma, high sum, low sum; row R is
-  // the padding target), flag bits, then [kStages][W] potential blocks, the
-  // mbarriers and the abort word
-  uint32_t* flags = reinterpret_cast<uint32_t*>(smem + rows_flags_off(a.R));
-  float* pot = reinterpret_cast<float*>(smem + rows_smem(a.R));
-  unsigned long long* bars = reinterpret_cast<unsigned long long*>(
-      smem + rows_smem(a.R) + (size_t)kStages * W * 4);
+  // the potential ring, the row state, the flag bits, the mbarriers and the
+  // abort word at their fixed offsets
+  uint32_t* flags = reinterpret_cast<uint32_t*>(smem + kFlagOff);
+  unsigned long long* bars = reinterpret_cast<unsigned long long*>(smem + kBarOff);
   volatile int* abort_w = reinterpret_cast<volatile int*>(bars + 2 * kStages);
   // bars, kStages each: potential block full, potential block empty
   const uint32_t bar0 = smem_u32(bars);
@@ -1125,7 +1187,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
         const int64_t c0 = (int64_t)b * W;
         const int64_t cnt = std::min<int64_t>(W, a.m_o - c0);
         const int64_t body = cnt & ~int64_t(3);
-        float* dst = pot + (size_t)sb * W;
+        float* dst = reinterpret_cast<float*>(smem + (size_t)sb * kStageBytes);
         // the last few floats when the block is not a multiple of 16 bytes
         for (int64_t q = body; q < cnt; ++q) dst[q] = a.other[c0 + q];
         mbar_arrive_tx(pot_full(sb), (uint32_t)(body * 4));
@@ -1180,15 +1242,15 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       const int r = r0 + lane;
       bool longrow = false;
       if (r <= a.R) {
-        uint32_t* st = row_state(smem, (uint32_t)r);
+        const uint32_t roff = 4u * (uint32_t)r;
         float sg = 0.0f;
         if (r < rows && OUT != kOutMax) {
           sg = a.sigma ? a.sigma[row0 + r] : __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
           longrow = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
         }
-        st[0] = __float_as_uint(sg);
-        st[1] = 0u;
-        st[2] = 0u;
+        *row_sigma(smem, roff) = sg;
+        *row_hi(smem, roff) = 0u;
+        *row_lo(smem, roff) = 0u;
       }
       const uint32_t word = __ballot_sync(0xffffffffu, longrow);
       if (lane == 0) flags[r0 >> 5] = word;
@@ -1200,7 +1262,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     // warp's first of the next tile) is in flight.  tile starts: e0, e1 bound
     // tile b, f1n the end of tile b + 1 (loaded a tile ahead of its use, so no
     // tile waits on a global load of its bounds)
-    constexpr int kStep = kGroup * kConsumerWarps;
     int64_t e0 = a.tstart[pb], e1 = a.tstart[pb + 1];
     int64_t f1n = a.B > 1 ? a.tstart[pb + 2] : e1;
     uint2 en[kGroup];
@@ -1223,20 +1284,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
       const int s = sb;
       if (!(ok = warp_wait(pot_full(s), ub, abort_w, a.err, 3))) break;
       if (++sb == kStages) { sb = 0; ub ^= 1u; }
-      const float* cur = pot + (size_t)s * W;
-      for (int g = kGroup * warp; g < nsl; g += kStep) {
-        uint2 e[kGroup];
-#pragma unroll
-        for (int j = 0; j < kGroup; ++j) e[j] = en[j];
-        if (g + kStep < nsl)
-          load_group(a.ent, e0, nsl, g + kStep, lane, en);
-        else
-          load_group(a.ent, f0, nsl_next, kGroup * warp, lane, en);
-        if (OUT == kOutMax)
-          process_group_max(smem, cur, e, nsl - g);
-        else
-          process_group(smem, flags, cur, e, nsl - g, capd);
-      }
+      consume_stage<OUT>(s, smem, flags, a.ent, e0, nsl, f0, nsl_next, warp, lane, capd, en);
       __syncwarp();
       if (lane == 0) mbar_arrive(pot_empty(s));
       e0 = f0;
@@ -1246,19 +1294,20 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     if (*abort_w) break;
     for (int r = tid; r < rows; r += kConsumers) {
       const int64_t seg = row0 + r;
-      const uint32_t* st = row_state(smem, (uint32_t)r);
+      const uint32_t roff = 4u * (uint32_t)r;
+      const uint32_t hi = *row_hi(smem, roff);
       if (OUT == kOutMax) {
-        a.out[seg] = st[1] ? radix_to_float(st[1]) : -INFINITY;
+        a.out[seg] = hi ? radix_to_float(hi) : -INFINITY;
         continue;
       }
-      const unsigned long long q = ((unsigned long long)st[1] << kLoBits) + st[2];
+      const unsigned long long q = ((unsigned long long)hi << kLoBits) + *row_lo(smem, roff);
       const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
       if (flagged || q < kFixMin) {
         a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
         continue;
       }
       const float tot = (float)((double)q * kFixInv);
-      const float lse = __fadd_rn(__uint_as_float(st[0]), logf(tot));
+      const float lse = __fadd_rn(*row_sigma(smem, roff), logf(tot));
       segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
                                  chk_bits, a.peers);
     }

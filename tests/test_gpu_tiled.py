@@ -119,7 +119,7 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     nnz = idx.numel()
     layout = build_tiles(ptr, idx, lam, n, m).cpu().numpy()
     P, R, B, logW, smem = _geometry(n, m, nnz)
-    assert smem <= 227 * 1024 and R < 65536 and P * R >= n and B << logW >= m
+    assert smem <= 227 * 1024 and R < 16384 and logW <= 14 and P * R >= n and B << logW >= m
     T = P * B
     cap = nnz + 63 * T
     off = _align(64)
@@ -141,8 +141,10 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     slabs += (slabs > 0) & (slabs % 2 == 0)  # an odd number of slabs
     padded = slabs * 32
     np.testing.assert_array_equal(tstart, np.concatenate([[0], np.cumsum(padded)]))
-    # padding: the dummy row R, column 0, lam = -inf
-    want_meta = np.full(cap, R << 16, dtype=np.uint64)
+    # meta = (row within panel) * 4 << 16 | (column within block) * 4 (byte
+    # offsets into the kernel's shared-memory arrays); padding: the dummy row R,
+    # column 0, lam = -inf
+    want_meta = np.full(cap, R << 18, dtype=np.uint64)
     want_lam = np.full(cap, -np.inf, dtype=np.float32)
     ustart = np.concatenate([[0], np.cumsum(counts)])
     t_o = tile_of[order]
@@ -151,7 +153,7 @@ def test_layout_holds_the_csr_tile_by_tile(cuda, n, m, L):
     ns = padded[t_o] // 32
     # sorted position p of a tile with N slabs: slab p mod N, lane p // N
     pos = tstart[t_o] + 32 * (p % ns) + p // ns
-    want_meta[pos] = ((row_of[order] % R) << 16) | (idx_h[order] & ((1 << logW) - 1))
+    want_meta[pos] = ((row_of[order] % R) << 18) | ((idx_h[order] & ((1 << logW) - 1)) << 2)
     want_lam[pos] = lam_h[order]
     np.testing.assert_array_equal(meta, want_meta.astype(np.uint32))
     np.testing.assert_array_equal(tlam, want_lam)
