@@ -236,6 +236,20 @@ def max_over_ranks(v: float, world: int, dev) -> float:
     return float(t.item())
 
 
+# launches per half-step of each side kind: the exact kernel; the staged tiled
+# pass + the exact pass over handed-back rows; the two-pass kind's exponent
+# pass, sum pass and handed-back pass
+SIDE_LAUNCHES = {"exact": 1, "staged": 2, "two_pass": 3}
+
+
+def side_kind(layout, nseg: int, m_other: int, nnz: int) -> str:
+    """How a side runs: "exact" (no tiled layout), "staged" or "two_pass"."""
+    if layout is None:
+        return "exact"
+    from sinkslot_b200.sinkhorn_solvers import tiles_kind_of
+    return tiles_kind_of(nseg, m_other, nnz)
+
+
 # --------------------------------------------------------------------------
 # the B200 arm
 # --------------------------------------------------------------------------
@@ -283,6 +297,8 @@ def run_b200(args):
     setup_cold_ms, setup_ms = setup_times
     nnz = int(rows.numel())
     csr = (r_ptr, r_idx, r_lam, c_ptr, c_idx, c_lam, log_a, log_b, w["n"], w["m"])
+    sides = {"row": side_kind(tiles[0] if tiles else None, w["n"], w["m"], nnz),
+             "col": side_kind(tiles[1] if tiles else None, w["m"], w["n"], nnz)}
 
     # warm-up, then exactly K timed iterations in one fused-loop call
     sinkslot_alternating_b200(*csr, max(args.warmup, 0), tiles=tiles)
@@ -393,8 +409,11 @@ def run_b200(args):
                          "peak_source": peak_kind,
                          "traffic": traffic.get("bytes_per_launch") if traffic else None,
                          "kernel": ("half_step_kernel (exact)" if args.plain else
-                                    "tiled_half_step_kernel + exact pass over handed-back rows")
+                                    "tiled half-step (staged: tiled_half_step_kernel; two-pass: "
+                                    "block_gather_kernel + panel_sum_kernel) + exact pass over "
+                                    "handed-back rows")
                                    + ", per half-step, averaged over the timed region",
+                         "sides": sides,
                          "bytes_per_half_step": {"row": bytes_row, "col": bytes_col},
                          "half_step_us": round(t_half * 1e6, 2),
                          "exact_kernel_us": {"row": round(t_row * 1e6, 2),
@@ -406,9 +425,10 @@ def run_b200(args):
                     "d2h_bytes_per_step": d2h,
                     "step": "sinkslot_solve(...) from pinned host x, y, a, b: support build + "
                             "%d iterations + potentials back" % w["n_iters"]},
-            # first iteration: the row side's exact launch, the column side's max pass,
-            # tiled pass and exact pass; later ones: tiled + exact pass per side
-            "gpu_launches": 2 * args.steps if args.plain else 4 * args.steps,
+            # per iteration the launches of each side's kind (the first iteration's
+            # row half-step is one exact launch, its column side adds a max pass)
+            "gpu_launches": args.steps * (SIDE_LAUNCHES[sides["row"]] +
+                                          SIDE_LAUNCHES[sides["col"]]),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -461,8 +481,8 @@ def run_b200_sharded(args, world, rank, local):
     t_half = ms / 1e3 / (2 * args.steps)
     # this rank's bytes per half-step: its slice's entries and segments
     r_nnz, c_nnz = solver.row[3], solver.col[3]
-    sides = {"row": "tiled" if solver.r_tiles is not None else "exact",
-             "col": "tiled" if solver.c_tiles is not None else "exact"}
+    sides = {"row": side_kind(solver.r_tiles, solver.nr, w["m"], r_nnz),
+             "col": side_kind(solver.c_tiles, solver.nc, w["n"], c_nnz)}
     bytes_row = r_nnz * (solver.row[1].element_size() + 4) + 16 * solver.nr
     bytes_col = c_nnz * (solver.col[1].element_size() + 4) + 16 * solver.nc
     achieved = max_over_ranks(-((bytes_row + bytes_col) / (2 * t_half) / 1e9), world, dev)
@@ -531,8 +551,9 @@ def run_b200_sharded(args, world, rank, local):
                     "d2h_bytes_per_step": d2h,
                     "step": "sinkslot_solve_sharded(...) from pinned host x, y, a, b: support "
                             "build + %d iterations + potentials back" % w["n_iters"]},
-            # first iteration: exact + push + wait per side; later: tiled + exact + push + wait
-            "gpu_launches": 6 + 8 * (args.steps - 1),
+            # per half-step: the side's kernels + peer publish + epoch wait
+            "gpu_launches": args.steps * (SIDE_LAUNCHES[sides["row"]] +
+                                          SIDE_LAUNCHES[sides["col"]] + 4),
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -896,10 +917,9 @@ def run_cfg5(args):
         _, ms = _timed(stream, lambda: sinkslot_alternating_b200(*csr, K, tiles=tl))
         clocks = sampler.stop()
         b_iter = _side_bytes(csr[1], nnz, n) + _side_bytes(csr[4], nnz, m)
-        sides = {"row": "tiled" if tl[0] is not None else "exact",
-                 "col": "tiled" if tl[1] is not None else "exact"}
+        sides = {"row": side_kind(tl[0], n, m, nnz), "col": side_kind(tl[1], m, n, nnz)}
         achieved = b_iter * K / (ms / 1e3) / 1e9
-        launches = 2 * K  # one exact or tiled pass per half-step (+ its handed-back pass)
+        launches = K * (SIDE_LAUNCHES[sides["row"]] + SIDE_LAUNCHES[sides["col"]])
         del csr, tl
         torch.cuda.empty_cache()
     else:
@@ -929,11 +949,11 @@ def run_cfg5(args):
         ms = max_over_ranks(ms, world, dev)
         b_iter = (_side_bytes(solver.row[1], solver.row[3], solver.nr) +
                   _side_bytes(solver.col[1], solver.col[3], solver.nc))
-        sides = {"row": "tiled" if solver.r_tiles is not None else "exact",
-                 "col": "tiled" if solver.c_tiles is not None else "exact"}
+        sides = {"row": side_kind(solver.r_tiles, solver.nr, m, solver.row[3]),
+                 "col": side_kind(solver.c_tiles, solver.nc, n, solver.col[3])}
         achieved = -max_over_ranks(-(b_iter * K / (ms / 1e3) / 1e9), world, dev)
-        # per half-step: the pass over the rank's slice, the publish, the epoch wait
-        launches = 6 * K
+        # per half-step: the side's kernels over the rank's slice, the publish, the epoch wait
+        launches = K * (SIDE_LAUNCHES[sides["row"]] + SIDE_LAUNCHES[sides["col"]] + 4)
         solver.close()
         del solver
         torch.cuda.empty_cache()
@@ -1148,7 +1168,12 @@ def main():
     ap.add_argument("--log2n", type=int, default=20,
                     help="points per cloud = 2^log2n (20: the headline problem; smaller sizes "
                          "are for profiling captures)")
+    ap.add_argument("--tiles-kind", choices=["auto", "staged", "two_pass"], default="auto",
+                    help="how sides with a tiled layout run (auto: by the cost of staging)")
     args = ap.parse_args()
+    if args.impl == "b200" and args.tiles_kind != "auto":
+        from sinkslot_b200.sinkhorn_solvers import set_tiles_kind
+        set_tiles_kind(args.tiles_kind)
     if args.log2n != 20:
         global WORKLOAD_NAME
         WORKLOAD["n"] = WORKLOAD["m"] = 1 << args.log2n

@@ -180,6 +180,28 @@ int sinkslot_tiles_bytes(int64_t nseg, int64_t m_other, int64_t nnz, int64_t* la
  * cap = nnz + 63*P*B. */
 int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geom_host);
 
+/* How the half-step uses a tiled layout (no counterpart in the reference):
+ * 1 staged -- one pass; each panel's CTA copies every block of the gathered
+ * potential into shared memory (P * m_other * 4 bytes per half-step); 2
+ * two-pass -- one CTA per block stages it once and stores each entry's
+ * exponent lam + potential in layout order, then one CTA per panel sums its
+ * entries with no gather (16 bytes per entry, all streamed; for gathered axes
+ * too long to stage once per panel); 0 auto (the default) -- staged while
+ * P * m_other * 4 <= 6 * nnz * 8, else two-pass.  The setting is process-wide
+ * and read whenever a layout's geometry is computed (sinkslot_tiles_bytes,
+ * sinkslot_tiles_geometry, sinkslot_build_tiles, the solve entry points): a
+ * layout must be built and used under the same setting.  A two-pass layout is
+ * the staged one followed by uint16 row byte offsets[cap], float
+ * exponents[cap], uint16 column byte offsets[cap] and float lam[cap] (each
+ * slot's entry split by what each pass reads; each part 256-byte aligned);
+ * header[1..3] of every layout
+ * hold its kind, P and B, and a half-step given a layout of another kind or
+ * geometry fails with an error status instead of reading it. */
+int sinkslot_set_tiles_kind(int kind);
+int sinkslot_get_tiles_kind(int* kind_host);
+/* The kind (1 or 2) a layout of these sizes gets under the current setting. */
+int sinkslot_tiles_kind_of(int64_t nseg, int64_t m_other, int64_t nnz, int* kind_host);
+
 /* Column-blocked layout of a CSR side for the shared-memory-staged half-step
  * (no counterpart in the reference: a layout of its CSR, `to_csr`,
  * sinkslot/solver.py:235-276, built once per solve). */

@@ -70,6 +70,9 @@ _SIGNATURES = {
                              ctypes.POINTER(ctypes.c_uint32), c_vp, c_i64, P_dbl, P_dbl, c_vp],
     "sinkslot_tiles_bytes": [c_i64, c_i64, c_i64, P_i64, P_i64],
     "sinkslot_tiles_geometry": [c_i64, c_i64, c_i64, P_int],
+    "sinkslot_set_tiles_kind": [c_int],
+    "sinkslot_get_tiles_kind": [P_int],
+    "sinkslot_tiles_kind_of": [c_i64, c_i64, c_i64, P_int],
     "sinkslot_build_tiles": [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp,
                              c_i64, c_vp],
     "sinkslot_plan_values": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_dbl, c_int,

@@ -293,6 +293,28 @@ int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geo
   return kOk;
 }
 
+int sinkslot_set_tiles_kind(int kind) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(kind == kTilesAuto || kind == kTilesStaged || kind == kTilesTwoPass,
+                   "set_tiles_kind: kind must be 0 (auto), 1 (staged) or 2 (two-pass)");
+  set_tiles_kind(kind);
+  return kOk;
+}
+
+int sinkslot_get_tiles_kind(int* kind_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(kind_host != nullptr, "get_tiles_kind: null argument");
+  *kind_host = tiles_kind();
+  return kOk;
+}
+
+int sinkslot_tiles_kind_of(int64_t nseg, int64_t m_other, int64_t nnz, int* kind_host) {
+  g_last_error_clear();
+  SINKSLOT_REQUIRE(kind_host && nseg >= 1 && m_other >= 1 && nnz >= 0, "tiles_kind_of: bad args");
+  *kind_host = tile_geom(nseg, m_other, nnz, num_sms()).kind;
+  return kOk;
+}
+
 int sinkslot_build_tiles(const int32_t* indptr, const void* idx, int idx_bytes, const float* lam,
                          int64_t nseg, int64_t m_other, int64_t nnz, void* layout,
                          int64_t layout_bytes, void* workspace, int64_t workspace_bytes,

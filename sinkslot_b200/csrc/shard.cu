@@ -281,9 +281,11 @@ int shard_loop(const ShardSpec& sp, int64_t it0, int64_t n_iters, int check, int
   uint32_t h[8];
   SINKSLOT_TRY(read_words(acc, h, sizeof(h), st));
   if (h[4] != 0) {
-    set_error(h[4] == 5 ? "solve_shard: a peer did not publish its potentials in time (code 5)"
-                        : "solve_shard: a shared-memory pipeline wait timed out (code " +
-                              std::to_string(h[4]) + ")");
+    set_error(h[4] == 5   ? "solve_shard: a peer did not publish its potentials in time (code 5)"
+              : h[4] == 4 ? "solve_shard: a tiled layout was built for another kind or geometry "
+                            "(code 4); build and solve under the same tiles kind"
+                          : "solve_shard: a shared-memory pipeline wait timed out (code " +
+                                std::to_string(h[4]) + ")");
     return kCudaError;
   }
   float f0, f1;

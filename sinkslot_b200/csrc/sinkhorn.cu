@@ -224,8 +224,10 @@ static int read_err(const int* d_err, cudaStream_t st) {
   SINKSLOT_CUDA_TRY(cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
   SINKSLOT_CUDA_TRY(cudaStreamSynchronize(st));
   if (h != 0) {
-    set_error("tiled half-step: a shared-memory pipeline wait timed out (code " +
-              std::to_string(h) + ")");
+    set_error(h == 4 ? std::string("tiled half-step: the layout was built for another kind or "
+                                   "geometry (code 4); build and solve under the same tiles kind")
+                     : "tiled half-step: a shared-memory pipeline wait timed out (code " +
+                           std::to_string(h) + ")");
     return kCudaError;
   }
   return kOk;

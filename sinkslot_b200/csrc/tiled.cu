@@ -159,34 +159,78 @@ static size_t direct_smem(int Rs, int B) {
          64;
 }
 
-TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
-  TileGeom g;
-  g.nseg = nseg;
-  g.m_o = m_o;
-  g.nnz = nnz;
-  if (nseg <= 0 || m_o <= 0) return g;
+// Two-pass kind: the panel-sum pass keeps only the row state in shared memory
+// (no potential ring), so a panel holds up to kRowCap2 - 1 rows (row byte
+// offsets stay 16-bit); the block-gather pass stages one block per CTA.
+constexpr uint32_t kRowCap2 = 16384;
+constexpr uint32_t kSigOff2 = 0;
+constexpr uint32_t kHiOff2 = 4 * kRowCap2;
+constexpr uint32_t kLoOff2 = 8 * kRowCap2;
+constexpr uint32_t kFlagOff2 = 12 * kRowCap2;
+constexpr uint32_t kAbortOff2 = kFlagOff2 + kRowCap2 / 8;
+constexpr size_t kSumSmem = kAbortOff2 + 16;
+static_assert(kSumSmem <= kSmemCap, "panel-sum kernel shared memory");
+
+// A side runs the staged kind when staging the gathered potential costs at most
+// this many times its entry stream: each of the P panels copies all m_o
+// potentials into shared memory per half-step (P * m_o * 4 bytes) while the
+// entries are read once (nnz * 8 bytes).  Above it the two-pass kind (16
+// bytes per entry, all streamed) is cheaper.  Measured on B200 (N = M = 2^k,
+// half-step us staged / two-pass): 2^21 (ratio 2.3) 292 / 508, 2^22 (ratio
+// 4.6) 964 / 1067; at 2^24 (ratio 20) the two-pass kind runs 165 iterations/s
+// against the exact kernel's 108.
+#ifndef SINKSLOT_STAGING_RATIO
+#define SINKSLOT_STAGING_RATIO 6.0
+#endif
+
+static int g_tiles_kind = kTilesAuto;
+void set_tiles_kind(int kind) { g_tiles_kind = kind; }
+int tiles_kind() { return g_tiles_kind; }
+
+static void panel_split(TileGeom& g, int64_t nseg, int sms, uint32_t row_cap) {
   int64_t P = sms;
   if (nseg < P * 32) P = std::max<int64_t>(1, ceil_div64(nseg, 32));
   int64_t R = ceil_div64(nseg, P);
   // the panel's rows and the dummy row within the row state (more panels per SM)
-  while (R + 1 > (int64_t)kRowCap) {
+  while (R + 1 > (int64_t)row_cap) {
     P += sms;
     R = ceil_div64(nseg, P);
   }
+  g.P = (int)P;
+  g.R = (int)R;
+}
+
+TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms, int kind) {
+  TileGeom g;
+  g.nseg = nseg;
+  g.m_o = m_o;
+  g.nnz = nnz;
+  if (kind < 0) kind = g_tiles_kind;
+  if (nseg <= 0 || m_o <= 0) return g;
+  panel_split(g, nseg, sms, kRowCap);
+  if (kind == kTilesAuto)
+    kind = (double)g.P * (double)m_o * 4.0 <= SINKSLOT_STAGING_RATIO * (double)nnz * 8.0
+               ? kTilesStaged : kTilesTwoPass;
+  g.kind = kind == kTilesTwoPass ? kTilesTwoPass : kTilesStaged;
+  if (g.kind == kTilesTwoPass) panel_split(g, nseg, sms, kRowCap2);
   // the widest block (fewest tiles), up to a ring stage
   int logW = 2;
   while (logW < kMaxLogW && ((int64_t)1 << logW) < m_o) ++logW;
-  g.P = (int)P;
-  g.R = (int)R;
   g.logW = logW;
   g.B = (int)ceil_div64(m_o, (int64_t)1 << logW);
-  g.smem_bytes = kTileSmem;
+  g.smem_bytes = g.kind == kTilesTwoPass ? kSumSmem : kTileSmem;
   const int64_t ntiles = (int64_t)g.P * g.B;
   g.cap = nnz + (2 * kSlab - 1) * ntiles;  // each tile: an odd number of slabs
   Carver cv(nullptr, 0);
-  cv.take<int64_t>(8);            // header: [0] longest row of <= kMaxTiledRow entries
+  cv.take<int64_t>(8);            // header: longest row, kind, P, B
   cv.take<int64_t>(ntiles + 1);   // tile starts (padded)
   cv.take<uint2>(std::max<int64_t>(g.cap, 1));  // entries {meta, lam bits}
+  if (g.kind == kTilesTwoPass) {
+    cv.take<uint16_t>(std::max<int64_t>(g.cap, 1));  // row byte offset per slot
+    cv.take<float>(std::max<int64_t>(g.cap, 1));     // exponent lam + potential per slot
+    cv.take<uint16_t>(std::max<int64_t>(g.cap, 1));  // column byte offset per slot
+    cv.take<float>(std::max<int64_t>(g.cap, 1));     // lam per slot
+  }
   g.layout_bytes = cv.used;
   g.S = (int)std::min<int64_t>(16, std::max<int64_t>(1, ceil_div64((int64_t)kBuildCtasPerSm * sms,
                                                                      g.P)));
@@ -210,9 +254,13 @@ TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms) {
 }
 
 struct LayoutPtrs {
-  int64_t* header;
+  int64_t* header;  // [0] longest row of <= kMaxTiledRow entries, [1] kind, [2] P, [3] B
   int64_t* tstart;
   uint2* ent;
+  uint16_t* rowoff;  // two-pass kind: row byte offset per slot (ent.x >> 16)
+  float* expo;       // two-pass kind: exponent lam + potential per slot
+  uint16_t* coloff;  // two-pass kind: column byte offset per slot (ent.x & 0xFFFF)
+  float* lamv;       // two-pass kind: lam per slot (ent.y)
 };
 
 static LayoutPtrs carve_layout(void* layout, const TileGeom& g) {
@@ -221,6 +269,16 @@ static LayoutPtrs carve_layout(void* layout, const TileGeom& g) {
   p.header = cv.take<int64_t>(8);
   p.tstart = cv.take<int64_t>((int64_t)g.P * g.B + 1);
   p.ent = cv.take<uint2>(std::max<int64_t>(g.cap, 1));
+  p.rowoff = nullptr;
+  p.expo = nullptr;
+  p.coloff = nullptr;
+  p.lamv = nullptr;
+  if (g.kind == kTilesTwoPass) {
+    p.rowoff = cv.take<uint16_t>(std::max<int64_t>(g.cap, 1));
+    p.expo = cv.take<float>(std::max<int64_t>(g.cap, 1));
+    p.coloff = cv.take<uint16_t>(std::max<int64_t>(g.cap, 1));
+    p.lamv = cv.take<float>(std::max<int64_t>(g.cap, 1));
+  }
   return p;
 }
 
@@ -336,6 +394,28 @@ __global__ void tile_scatter_kernel(const uint32_t* __restrict__ skey,
 }
 
 static int place_column_banks(const TileGeom& g, const LayoutPtrs& L, cudaStream_t st);
+
+// header: [0] longest row (raised by the builder), [1] kind, [2] P, [3] B; the
+// half-step kernels compare [1..3] with their own geometry
+__global__ void layout_header_kernel(int64_t* __restrict__ header, int kind, int P, int B) {
+  const int i = threadIdx.x;
+  if (i < 8) header[i] = i == 1 ? kind : i == 2 ? P : i == 3 ? B : 0;
+}
+
+// two-pass kind: every slot's entry split into what each pass reads (padding
+// included) -- the row byte offset for the panel-sum pass, the column byte
+// offset and lam for the block-gather pass
+__global__ void split_slots_kernel(const uint2* __restrict__ ent, int64_t cap,
+                                   uint16_t* __restrict__ rowoff, uint16_t* __restrict__ coloff,
+                                   float* __restrict__ lamv) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < cap;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const uint2 e = ent[q];
+    rowoff[q] = (uint16_t)(e.x >> 16);
+    coloff[q] = (uint16_t)(e.x & 0xFFFFu);
+    lamv[q] = __uint_as_float(e.y);
+  }
+}
 
 // ---------------------------------------------------------------------------
 // direct builder: one CTA per sub-panel, no sort
@@ -600,7 +680,8 @@ static int build_tiles_direct(const int32_t* ptr, const IT* idx, const float* la
     }
   }
   const dim3 grid((unsigned)g.S, (unsigned)g.P);
-  SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.header, 0, 8 * sizeof(int64_t), st));
+  layout_header_kernel<<<1, 32, 0, st>>>(L.header, g.kind, g.P, g.B);
+  SINKSLOT_CHECK_LAUNCH();
   panel_count_kernel<IT><<<grid, kBuildThreads, smem, st>>>(
       ptr, idx, g.nseg, g.R, Rs, g.B, g.logW, cnt,
       reinterpret_cast<unsigned long long*>(L.header));
@@ -758,8 +839,9 @@ static int place_column_banks(const TileGeom& g, const LayoutPtrs& L, cudaStream
   return kOk;
 }
 
-int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float* lam,
-                const TileGeom& g, void* layout, void* ws, size_t ws_bytes, cudaStream_t st) {
+static int build_tiles_body(const int32_t* ptr, const void* idx, int idx_bytes,
+                            const float* lam, const TileGeom& g, void* layout, void* ws,
+                            size_t ws_bytes, cudaStream_t st) {
   SINKSLOT_REQUIRE(idx_bytes == 2 || idx_bytes == 4, "build_tiles: idx_bytes must be 2 or 4");
   SINKSLOT_REQUIRE(g.nnz < (int64_t(1) << 32), "build_tiles: nnz must be < 2^32");
   SINKSLOT_REQUIRE(g.P > 0 && g.B > 0, "build_tiles: empty geometry");
@@ -787,7 +869,8 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
     set_error("build_tiles: workspace too small");
     return kWorkspaceTooSmall;
   }
-  SINKSLOT_CUDA_TRY(cudaMemsetAsync(L.header, 0, 8 * sizeof(int64_t), st));
+  layout_header_kernel<<<1, 32, 0, st>>>(L.header, g.kind, g.P, g.B);
+  SINKSLOT_CHECK_LAUNCH();
   fill_pad_kernel<<<grid_t(g.cap, 256), 256, 0, st>>>(L.ent, g.cap, g.R);
   SINKSLOT_CHECK_LAUNCH();
   rowid_kernel<<<grid_t(g.nseg, 256), 256, 0, st>>>(
@@ -825,6 +908,18 @@ int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float*
         L.tstart, L.ent);
   SINKSLOT_CHECK_LAUNCH();
   return place_column_banks(g, L, st);
+}
+
+int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float* lam,
+                const TileGeom& g, void* layout, void* ws, size_t ws_bytes, cudaStream_t st) {
+  SINKSLOT_TRY(build_tiles_body(ptr, idx, idx_bytes, lam, g, layout, ws, ws_bytes, st));
+  if (g.kind == kTilesTwoPass) {
+    const LayoutPtrs L = carve_layout(layout, g);
+    split_slots_kernel<<<grid_t(g.cap, 256), 256, 0, st>>>(L.ent, g.cap, L.rowoff, L.coloff,
+                                                           L.lamv);
+    SINKSLOT_CHECK_LAUNCH();
+  }
+  return kOk;
 }
 
 // ---------------------------------------------------------------------------
@@ -942,6 +1037,8 @@ struct TKArgs {
   int* err;
   PeerOut peers;
   unsigned int* done;
+  const uint16_t* rowoff;  // two-pass kind: row byte offset per slot
+  const float* expo;       // two-pass kind: exponent lam + potential per slot
 };
 
 // The state words of panel row r, addressed by its byte offset 4 r (the high
@@ -1131,6 +1228,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  // a layout built for another kind or geometry: fail (the host reports it)
+  if (a.header[1] != kTilesStaged || a.header[2] != a.P || a.header[3] != a.B) {
+    chain_enter();
+    if (tid == 0) atomicCAS(a.err, 0, 4);
+    return;
+  }
   // The kernel may start while the previous launch of the loop is finishing
   // (programmatic dependent launch).  Before chain_enter it touches only what
   // no running launch writes: its shared memory, the layout, and (consumers,
@@ -1322,6 +1425,369 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// two-pass kind
+// ---------------------------------------------------------------------------
+// When the gathered axis is too long to stage once per panel (P * m_o * 4
+// bytes per half-step), the half-step runs in two streaming passes over the
+// same layout:
+//   block_gather_kernel: CTA (b, q) copies block b of the gathered potential
+//     into shared memory once and walks the tiles (p, b) of the panels p of
+//     chunk q, one warp per tile; each slot's exponent lam + potential[column]
+//     is stored at the slot's own index of the exponent array (coalesced
+//     8-byte loads, 4-byte stores; padding slots give -inf);
+//   panel_sum_kernel: one CTA per panel streams the panel's slots (tiles
+//     (p, 0 .. B-1) are contiguous) -- the row byte offset and the exponent --
+//     and sums exp(exponent - sigma) into the row state exactly as the staged
+//     kernel does (same fixed point, cap, hand-back rule and epilogue), so the
+//     two kinds give the same bits.  No gather and no potential ring: the whole
+//     shared memory holds row state (up to kRowCap2 - 1 rows per panel).
+// Bytes per slot and half-step: 2 + 4 read and 4 written, then 2 + 4 read (the
+// layout keeps each slot split into a row offset, a column offset and lam).
+constexpr int kGatherWarps = 16;
+constexpr int kGatherThreads = 32 * kGatherWarps;
+constexpr int kGatherCtasPerSm = 3;  // 64 KB blocks: three per SM
+constexpr int kGatherUnroll = 4;     // slabs a lane has in flight
+constexpr int kSumWarps = 32;
+constexpr int kSumThreads = 32 * kSumWarps;
+constexpr int kSumGroup = 8;         // slabs a warp loads together, one group ahead
+
+struct BGArgs {
+  int64_t m_o;
+  int P, B, logW, pchunk;
+  const int64_t* header;
+  const int64_t* tstart;
+  const uint16_t* coloff;
+  const float* lamv;
+  const float* other;
+  float* expo;
+  int* err;
+};
+
+__device__ __forceinline__ bool layout_matches(const int64_t* header, int kind, int P, int B) {
+  return header[1] == kind && header[2] == P && header[3] == B;
+}
+
+// slots [e0, e1) of the split arrays into L2 (tile ranges start on 32-slot
+// boundaries and span whole slabs: 64- and 128-byte multiples)
+__device__ __forceinline__ void prefetch_gather_tile(const uint16_t* coloff, const float* lamv,
+                                                     int64_t e0, int64_t e1) {
+  if (e1 <= e0) return;
+  prefetch_l2(coloff + e0, (uint32_t)(e1 - e0) * 2u);
+  prefetch_l2(lamv + e0, (uint32_t)(e1 - e0) * 4u);
+}
+
+__global__ void __launch_bounds__(kGatherThreads, kGatherCtasPerSm)
+    block_gather_kernel(const BGArgs a) {
+  extern __shared__ __align__(16) unsigned char potb[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (!layout_matches(a.header, kTilesTwoPass, a.P, a.B)) {
+    chain_enter();
+    if (tid == 0) atomicCAS(a.err, 0, 4);
+    return;
+  }
+  const int b = blockIdx.x;
+  const int p0 = blockIdx.y * a.pchunk;
+  const int p1 = min(a.P, p0 + a.pchunk);
+  // the warp's first tile: bounds now, slots into L2 while the previous launch
+  // finishes (the layout is static)
+  int p = p0 + warp;
+  int64_t e0 = 0, e1 = 0;
+  if (p < p1) {
+    e0 = a.tstart[(int64_t)p * a.B + b];
+    e1 = a.tstart[(int64_t)p * a.B + b + 1];
+    if (lane == 0) prefetch_gather_tile(a.coloff, a.lamv, e0, e1);
+  }
+  chain_enter();
+  if (*(volatile int*)a.err != 0) return;  // an earlier launch failed: do nothing
+  const int64_t c0 = (int64_t)b << a.logW;
+  const int cnt = (int)std::min<int64_t>((int64_t)1 << a.logW, a.m_o - c0);
+  float* pot = reinterpret_cast<float*>(potb);
+  for (int i = tid; i < cnt; i += kGatherThreads) pot[i] = a.other[c0 + i];
+  __syncthreads();
+  for (; p < p1; p += kGatherWarps) {
+    // the warp's next tile: bounds loaded and slots prefetched a tile ahead
+    const int pn = p + kGatherWarps;
+    int64_t f0 = 0, f1 = 0;
+    if (pn < p1) {
+      f0 = a.tstart[(int64_t)pn * a.B + b];
+      f1 = a.tstart[(int64_t)pn * a.B + b + 1];
+      if (lane == 0) prefetch_gather_tile(a.coloff, a.lamv, f0, f1);
+    }
+    const int nsl = (int)((e1 - e0) >> 5);
+    const uint16_t* cs = a.coloff + e0 + lane;
+    const float* ls = a.lamv + e0 + lane;
+    float* dst = a.expo + e0 + lane;
+    int s = 0;
+    for (; s + kGatherUnroll <= nsl; s += kGatherUnroll) {
+      uint32_t c[kGatherUnroll];
+      float l[kGatherUnroll];
+#pragma unroll
+      for (int j = 0; j < kGatherUnroll; ++j) {
+        c[j] = ld_stream(cs + (s + j) * kSlab);
+        l[j] = ld_stream(ls + (s + j) * kSlab);
+      }
+#pragma unroll
+      for (int j = 0; j < kGatherUnroll; ++j)
+        __stcs(dst + (s + j) * kSlab,
+               __fadd_rn(l[j], *reinterpret_cast<const float*>(potb + c[j])));
+    }
+    for (; s < nsl; ++s) {
+      const uint32_t c = ld_stream(cs + s * kSlab);
+      __stcs(dst + s * kSlab,
+             __fadd_rn(ld_stream(ls + s * kSlab), *reinterpret_cast<const float*>(potb + c)));
+    }
+    e0 = f0;
+    e1 = f1;
+  }
+  chain_release();
+}
+
+__device__ __forceinline__ float* row_sigma2(unsigned char* smem, uint32_t roff) {
+  return reinterpret_cast<float*>(smem + kSigOff2 + roff);
+}
+__device__ __forceinline__ uint32_t* row_hi2(unsigned char* smem, uint32_t roff) {
+  return reinterpret_cast<uint32_t*>(smem + kHiOff2 + roff);
+}
+__device__ __forceinline__ uint32_t* row_lo2(unsigned char* smem, uint32_t roff) {
+  return reinterpret_cast<uint32_t*>(smem + kLoOff2 + roff);
+}
+
+// slabs g .. g + kSumGroup - 1 (those below nsl) of the panel whose slots start
+// at e0: lane `lane`'s row offsets and exponents
+__device__ __forceinline__ void load_sum_group(const uint16_t* rowoff, const float* expo,
+                                               int64_t e0, int nsl, int g, int lane,
+                                               uint32_t (&ro)[kSumGroup],
+                                               float (&x)[kSumGroup]) {
+  const int64_t q = e0 + (int64_t)g * kSlab + lane;
+#pragma unroll
+  for (int j = 0; j < kSumGroup; ++j)
+    if (g + j < nsl) {
+      ro[j] = ld_stream(rowoff + q + j * kSlab);
+      x[j] = ld_stream(expo + q + j * kSlab);
+    }
+}
+
+// the slots of slabs g .. g + kSumGroup - 1 (below nsl) into L2
+__device__ __forceinline__ void prefetch_sum_group(const uint16_t* rowoff, const float* expo,
+                                                   int64_t e0, int nsl, int g) {
+  if (g >= nsl) return;
+  const int64_t q = e0 + (int64_t)g * kSlab;
+  const uint32_t n = (uint32_t)min(kSumGroup, nsl - g) * kSlab;
+  prefetch_l2(rowoff + q, n * 2u);
+  prefetch_l2(expo + q, n * 4u);
+}
+
+template <int OUT, int CHK>
+__global__ void __launch_bounds__(kSumThreads, 1) panel_sum_kernel(const TKArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint32_t* flags = reinterpret_cast<uint32_t*>(smem + kFlagOff2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (!layout_matches(a.header, kTilesTwoPass, a.P, a.B)) {
+    chain_enter();
+    if (tid == 0) atomicCAS(a.err, 0, 4);
+    return;
+  }
+  const long long longest = a.header[0] > 0 ? a.header[0] : 1;
+  int lg = 0;
+  while ((1ll << lg) < longest) ++lg;
+  const int k = kLoBits - lg;
+  // terms above 2^k would overflow the high-part sum of the longest row
+  const float capd = (longest <= kMaxTiledRow && k >= 1) ? ((float)k - 0.01f) * 0.69314718f
+                                                         : -INFINITY;
+  uint32_t chk_bits = 0;
+  // Before chain_enter the kernel reads only what no running launch writes:
+  // the layout, base, self_old (this side's own output, written at least four
+  // launches back) and the CSR offsets.  The exponents (the previous launch's
+  // output), the stabilisers of a max pass and the error word come after it.
+  bool entered = false;
+  if (a.sigma != nullptr) {
+    chain_enter();
+    entered = true;
+    if (a.fb_reset && blockIdx.x == 0 && tid == 0) *a.fb_reset = 0;
+  }
+  constexpr int kStep = kSumGroup * kSumWarps;
+  for (int p = blockIdx.x; p < a.P; p += gridDim.x) {
+    const int64_t row0 = (int64_t)p * a.R;
+    const int rows = (int)std::min<int64_t>(a.R, a.nseg - row0);
+    if (rows <= 0) break;
+    // row state and flag words (rows longer than kMaxTiledRow are handed back
+    // from the start)
+    for (int r0 = warp * 32; r0 <= a.R; r0 += kSumThreads) {
+      const int r = r0 + lane;
+      bool longrow = false;
+      if (r <= a.R) {
+        const uint32_t roff = 4u * (uint32_t)r;
+        float sg = 0.0f;
+        if (r < rows && OUT != kOutMax) {
+          sg = a.sigma ? a.sigma[row0 + r] : __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
+          longrow = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
+        }
+        *row_sigma2(smem, roff) = sg;
+        *row_hi2(smem, roff) = 0u;
+        *row_lo2(smem, roff) = 0u;
+      }
+      const uint32_t word = __ballot_sync(0xffffffffu, longrow);
+      if (lane == 0) flags[r0 >> 5] = word;
+    }
+    const int64_t e0 = a.tstart[(int64_t)p * a.B];
+    const int nsl = (int)((a.tstart[(int64_t)(p + 1) * a.B] - e0) >> 5);
+    if (!entered) {
+      chain_enter();
+      entered = true;
+      if (a.fb_reset && blockIdx.x == 0 && tid == 0) *a.fb_reset = 0;
+    }
+    // every thread reads the word after the previous launches completed: the
+    // same value in all threads
+    if (*(volatile int*)a.err != 0) break;
+    __syncthreads();
+    uint32_t ron[kSumGroup];
+    float xn[kSumGroup];
+    if (lane == 0) prefetch_sum_group(a.rowoff, a.expo, e0, nsl, kSumGroup * warp + kStep);
+    load_sum_group(a.rowoff, a.expo, e0, nsl, kSumGroup * warp, lane, ron, xn);
+    for (int g = kSumGroup * warp; g < nsl; g += kStep) {
+      uint32_t ro[kSumGroup];
+      float x[kSumGroup];
+#pragma unroll
+      for (int j = 0; j < kSumGroup; ++j) {
+        ro[j] = ron[j];
+        x[j] = xn[j];
+      }
+      if (lane == 0) prefetch_sum_group(a.rowoff, a.expo, e0, nsl, g + 2 * kStep);
+      load_sum_group(a.rowoff, a.expo, e0, nsl, g + kStep, lane, ron, xn);
+      const int cnt = nsl - g;
+      if (OUT == kOutMax) {
+#pragma unroll
+        for (int j = 0; j < kSumGroup; ++j)
+          if (j < cnt) atomicMax(row_hi2(smem, ro[j]), float_to_radix(x[j]));
+      } else if (cnt >= kSumGroup) {
+        float d[kSumGroup];
+        bool in_cap = true;
+#pragma unroll
+        for (int j = 0; j < kSumGroup; ++j) {
+          d[j] = __fsub_rn(x[j], *row_sigma2(smem, ro[j]));
+          in_cap &= d[j] <= capd;
+        }
+        if (!__all_sync(0xffffffffu, in_cap)) {
+#pragma unroll
+          for (int j = 0; j < kSumGroup; ++j)
+            if (!(d[j] <= capd)) {
+              const uint32_t r = ro[j] >> 2;
+              atomicOr(flags + (r >> 5), 1u << (r & 31));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kSumGroup; ++j) {
+          const unsigned long long q =
+              __float2ull_rn(exp2_approx(d[j] * 1.44269504088896341f) * kFixScale);
+          atomicAdd(row_hi2(smem, ro[j]), (uint32_t)(q >> kLoBits));
+          atomicAdd(row_lo2(smem, ro[j]), (uint32_t)q & ((1u << kLoBits) - 1u));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kSumGroup - 1; ++j) {
+          if (j < cnt) {
+            const float d = __fsub_rn(x[j], *row_sigma2(smem, ro[j]));
+            if (!(d <= capd)) {
+              const uint32_t r = ro[j] >> 2;
+              atomicOr(flags + (r >> 5), 1u << (r & 31));
+            }
+            const unsigned long long q =
+                __float2ull_rn(exp2_approx(d * 1.44269504088896341f) * kFixScale);
+            atomicAdd(row_hi2(smem, ro[j]), (uint32_t)(q >> kLoBits));
+            atomicAdd(row_lo2(smem, ro[j]), (uint32_t)q & ((1u << kLoBits) - 1u));
+          }
+        }
+      }
+    }
+    __syncthreads();
+    for (int r = tid; r < rows; r += kSumThreads) {
+      const int64_t seg = row0 + r;
+      const uint32_t roff = 4u * (uint32_t)r;
+      const uint32_t hi = *row_hi2(smem, roff);
+      if (OUT == kOutMax) {
+        a.out[seg] = hi ? radix_to_float(hi) : -INFINITY;
+        continue;
+      }
+      const unsigned long long q = ((unsigned long long)hi << kLoBits) + *row_lo2(smem, roff);
+      const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
+      if (flagged || q < kFixMin) {
+        a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
+        continue;
+      }
+      const float tot = (float)((double)q * kFixInv);
+      const float lse = __fadd_rn(*row_sigma2(smem, roff), logf(tot));
+      segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
+                                 chk_bits, a.peers);
+    }
+    __syncthreads();
+  }
+  if (!entered) chain_enter();
+  chain_release();
+  check_reduce<CHK>(chk_bits, a.acc);
+  if (a.peers.n > 0) {
+    __syncthreads();
+    peer_cta_done(a.peers, a.done);
+  }
+}
+
+static int launch_block_gather(const TiledHalfStep& h, cudaStream_t st) {
+  const TileGeom& g = h.g;
+  const LayoutPtrs L = carve_layout(const_cast<void*>(h.layout), g);
+  BGArgs a;
+  a.m_o = g.m_o;
+  a.P = g.P;
+  a.B = g.B;
+  a.logW = g.logW;
+  a.header = L.header;
+  a.tstart = L.tstart;
+  a.coloff = L.coloff;
+  a.lamv = L.lamv;
+  a.other = h.other;
+  a.expo = L.expo;
+  a.err = h.err;
+  // panel chunks: about four waves of CTAs in all (each restages its block)
+  const int64_t waves = 4 * (int64_t)kGatherCtasPerSm * num_sms();
+  int64_t Q = std::min<int64_t>(g.P, std::max<int64_t>(1, ceil_div64(waves, g.B)));
+  a.pchunk = (int)ceil_div64(g.P, Q);
+  Q = ceil_div64(g.P, a.pchunk);
+  SINKSLOT_REQUIRE(Q <= 65535, "two-pass half step: too many panel chunks");
+  const size_t smem = (size_t)4 << g.logW;
+  static bool configured[64] = {};
+  int dev = 0;
+  SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(block_gather_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)(4u << kMaxLogW)));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  SINKSLOT_CUDA_TRY(launch_chained(block_gather_kernel, dim3((unsigned)g.B, (unsigned)Q),
+                                   dim3(kGatherThreads), smem, st, a));
+  return kOk;
+}
+
+template <int OUT, int CHK>
+static int launch_panel_sum(const TKArgs& a, cudaStream_t st) {
+  static bool configured[64] = {};
+  int dev = 0;
+  SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(panel_sum_kernel<OUT, CHK>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kSumSmem));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int grid = std::min(a.P, num_sms());
+  SINKSLOT_CUDA_TRY(launch_chained(panel_sum_kernel<OUT, CHK>, dim3(grid), dim3(kSumThreads),
+                                   kSumSmem, st, a));
+  return kOk;
+}
+
+template <int OUT, int CHK>
+static int launch_tiled_kind(const TKArgs& a, const TileGeom& g, cudaStream_t st);
+
 template <int OUT, int CHK>
 static int launch_tiled(const TKArgs& a, size_t smem, cudaStream_t st) {
   // the dynamic shared-memory limit is a per-device function attribute
@@ -1368,6 +1834,8 @@ static TKArgs tk_args(const TiledHalfStep& h) {
   a.err = h.err;
   a.peers = h.peers;
   a.done = h.done;
+  a.rowoff = L.rowoff;
+  a.expo = L.expo;
   return a;
 }
 
@@ -1407,17 +1875,19 @@ int tiled_half_step(const TiledHalfStep& h, int out_mode, int chk, cudaStream_t 
                    "tiled half step: the gathered potential must be 16-byte aligned");
   if (h.g.nseg <= 0) return kOk;
   const TKArgs a = tk_args(h);
-  const size_t smem = h.g.smem_bytes;
+  // two-pass kind: the exponents first -- except after a max pass over the same
+  // potential (sigma given), which left them in place
+  if (h.g.kind == kTilesTwoPass && h.sigma == nullptr) SINKSLOT_TRY(launch_block_gather(h, st));
   if (out_mode == kOutPlain) {
-    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkNone>(a, smem, st)));
-    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled<kOutPlain, kChkMarg>(a, smem, st)));
-    else SINKSLOT_TRY((launch_tiled<kOutPlain, kChkPot>(a, smem, st)));
+    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled_kind<kOutPlain, kChkNone>(a, h.g, st)));
+    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled_kind<kOutPlain, kChkMarg>(a, h.g, st)));
+    else SINKSLOT_TRY((launch_tiled_kind<kOutPlain, kChkPot>(a, h.g, st)));
   } else if (out_mode == kOutBlend) {
-    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled<kOutBlend, kChkNone>(a, smem, st)));
-    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled<kOutBlend, kChkMarg>(a, smem, st)));
-    else SINKSLOT_TRY((launch_tiled<kOutBlend, kChkPot>(a, smem, st)));
+    if (chk == kChkNone) SINKSLOT_TRY((launch_tiled_kind<kOutBlend, kChkNone>(a, h.g, st)));
+    else if (chk == kChkMarg) SINKSLOT_TRY((launch_tiled_kind<kOutBlend, kChkMarg>(a, h.g, st)));
+    else SINKSLOT_TRY((launch_tiled_kind<kOutBlend, kChkPot>(a, h.g, st)));
   } else {
-    SINKSLOT_TRY((launch_tiled<kOutNone, kChkMarg>(a, smem, st)));
+    SINKSLOT_TRY((launch_tiled_kind<kOutNone, kChkMarg>(a, h.g, st)));
   }
   return exact_handed_back(h, out_mode, chk, st, ctas);
 }
@@ -1431,10 +1901,16 @@ int tiled_max_pass(const TiledHalfStep& h, float* sigma_out, cudaStream_t st, un
   a.out = sigma_out;
   a.peers.n = 0;
   a.fb_reset = nullptr;
-  SINKSLOT_TRY((launch_tiled<kOutMax, kChkNone>(a, h.g.smem_bytes, st)));
+  if (h.g.kind == kTilesTwoPass) SINKSLOT_TRY(launch_block_gather(h, st));
+  SINKSLOT_TRY((launch_tiled_kind<kOutMax, kChkNone>(a, h.g, st)));
   if (ctas) *ctas += (unsigned)std::min(h.g.P, num_sms());
   return kOk;
 }
 
+template <int OUT, int CHK>
+static int launch_tiled_kind(const TKArgs& a, const TileGeom& g, cudaStream_t st) {
+  if (g.kind == kTilesTwoPass) return launch_panel_sum<OUT, CHK>(a, st);
+  return launch_tiled<OUT, CHK>(a, g.smem_bytes, st);
+}
 
 }  // namespace sinkslot

@@ -9,6 +9,23 @@
 
 namespace sinkslot {
 
+// How a tiled layout is used by the half-step:
+//   kTilesStaged   one pass per half-step: each panel's CTA stages every block
+//                  of the gathered potential in shared memory (P * m_o * 4
+//                  bytes copied per half-step);
+//   kTilesTwoPass  two passes: one CTA per block stages it once and writes each
+//                  entry's exponent lam + potential in layout order, then one
+//                  CTA per panel sums its entries without a gather -- for
+//                  gathered axes too long to stage once per panel.
+// kTilesAuto picks by the cost of staging (tile_geom).
+enum TilesKind { kTilesAuto = 0, kTilesStaged = 1, kTilesTwoPass = 2 };
+
+// Process-wide kind used when a layout's geometry is computed (auto unless set):
+// a layout must be built and used under the same setting (the kernels check
+// the kind and geometry recorded in the layout's header and fail otherwise).
+void set_tiles_kind(int kind);
+int tiles_kind();
+
 // Geometry of a tiled layout: P panels of R rows; the gathered axis (length
 // m_o) cut into B blocks of W = 2^logW entries.  Tile (p, b) holds the entries
 // of panel p whose column falls in block b, padded to a multiple of 32 entries
@@ -23,9 +40,11 @@ struct TileGeom {
   size_t build_bytes = 0;   // scratch of the builder
   bool direct = false;      // built by the per-panel counting kernels (else by a sort)
   int S = 1;                // sub-panels (CTAs) per panel of the direct builder
+  int kind = kTilesStaged;  // kTilesStaged or kTilesTwoPass (never auto)
 };
 
-TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms);
+// kind: kTilesAuto / kTilesStaged / kTilesTwoPass, or -1 for tiles_kind()
+TileGeom tile_geom(int64_t nseg, int64_t m_o, int64_t nnz, int sms, int kind = -1);
 
 // Builds the layout (into `layout`, layout_bytes) from a CSR side.
 int build_tiles(const int32_t* ptr, const void* idx, int idx_bytes, const float* lam,

@@ -89,32 +89,51 @@ def _resolve_stop_mode(stop):
     return mode
 
 
-# A side runs the shared-memory-staged half-step when staging the gathered
-# potential costs at most this many times its entry stream: each of the P
-# panels copies all m_other potentials into shared memory per half-step
-# (P * m_other * 4 bytes) while the entries are read once (nnz * 8 bytes).
-# Measured on B200 (N = 2^20 on one GPU and 2^20 x 2^21 slices on two): the
-# tiled half-step costs ~165 us per GB of entries plus ~69 us per GB of
-# staging, the exact kernel ~590 us per GB of entries, so the tiled pass wins
-# below a ratio of ~6 (large gathered axes, e.g. N = 2^24, or row slices of a
-# many-GPU partition, run the exact kernel).
-TILE_STAGING_RATIO = 6.0
 # Below this many entries a half-step is a few microseconds of memory traffic:
-# the tiled kernel's fixed cost (a 1024-thread CTA per SM, barrier set-up, a
-# second launch for handed-back rows) outweighs its gain (measured at N = 10^4,
+# the tiled kernels' fixed cost (a 1024-thread CTA per SM, barrier set-up, a
+# second launch for handed-back rows) outweighs their gain (measured at N = 10^4,
 # L = 64: 22.9 us per iteration tiled, 14.4 us exact).
 TILE_MIN_NNZ = 1 << 22
+
+# How a side with a tiled layout runs (libsinkslot_b200 picks per side, by
+# sizes): "staged" stages every block of the gathered potential in shared
+# memory once per panel (one pass; P * m_other * 4 bytes copied per
+# half-step); "two_pass" first writes every entry's exponent lam + potential
+# with one CTA per block, then sums each panel's entries without a gather (16
+# bytes per entry, all streamed).  "auto" (the default) takes the staged kind
+# while its staging costs at most 6x the entry stream, else the two-pass kind:
+# large gathered axes (N = 2^24 on one GPU, row slices of a many-GPU partition)
+# no longer fall back to the exact kernel's random gathers (about 36 bytes of
+# HBM time per entry).
+TILES_KINDS = {"auto": 0, "staged": 1, "two_pass": 2}
+
+
+def set_tiles_kind(kind: str) -> None:
+    """Process-wide choice of the tiled half-step's kind ("auto", "staged",
+    "two_pass").  Layouts must be built and used under the same setting."""
+    if kind not in TILES_KINDS:
+        raise ValueError(f"tiles kind must be one of {tuple(TILES_KINDS)}, got {kind!r}")
+    call("sinkslot_set_tiles_kind", TILES_KINDS[kind])
+
+
+def get_tiles_kind() -> str:
+    k = ctypes.c_int(0)
+    call("sinkslot_get_tiles_kind", ctypes.byref(k))
+    return {v: n for n, v in TILES_KINDS.items()}[k.value]
+
+
+def tiles_kind_of(nseg: int, m_other: int, nnz: int) -> str:
+    """The kind ("staged" or "two_pass") a layout of these sizes gets now."""
+    k = ctypes.c_int(0)
+    call("sinkslot_tiles_kind_of", nseg, m_other, nnz, ctypes.byref(k))
+    return {1: "staged", 2: "two_pass"}[k.value]
 
 
 def tiles_pay_off(nseg: int, m_other: int, nnz: int) -> bool:
     """Whether a side of nseg segments gathering from m_other potentials with
-    nnz entries should run the tiled half-step (see TILE_STAGING_RATIO and
-    TILE_MIN_NNZ)."""
-    if nseg <= 0 or m_other <= 0 or nnz < TILE_MIN_NNZ:
-        return False
-    geom = (ctypes.c_int * 5)()
-    call("sinkslot_tiles_geometry", nseg, m_other, nnz, geom)
-    return geom[0] * m_other * 4 <= TILE_STAGING_RATIO * nnz * 8
+    nnz entries should run a tiled half-step (either kind) rather than the
+    exact kernel (see TILE_MIN_NNZ)."""
+    return nseg > 0 and m_other > 0 and nnz >= TILE_MIN_NNZ
 
 
 def build_tiles(indptr, idx, lam, nseg: int, m_other: int) -> torch.Tensor:

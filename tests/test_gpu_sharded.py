@@ -46,7 +46,7 @@ CASES = [
 ]
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, kind="auto"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -62,6 +62,8 @@ def _rank(rank, world, port, q):
         from sinkslot_b200 import sinkslot_solve
         from sinkslot_b200.sharded import sinkslot_solve_sharded
         sinkslot_b200.load_library()
+        from sinkslot_b200.sinkhorn_solvers import set_tiles_kind
+        set_tiles_kind(kind)  # every rank and the single-GPU solve alike
         out = []
         for n, m, variant, mode, eps, L in CASES:
             x, y, a, b = _inputs(n, m, 5, dev)
@@ -84,15 +86,18 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("kind", ["auto", "two_pass"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_sharded_solve_matches_single_gpu(world):
+def test_sharded_solve_matches_single_gpu(world, kind):
+    """kind "two_pass": the tiled sides (the first case's slices) run the
+    two-pass half-step, whose sum pass stores into the peers' buffers."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, kind)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
