@@ -187,7 +187,7 @@ int sinkslot_tiles_geometry(int64_t nseg, int64_t m_other, int64_t nnz, int* geo
  * exponent lam + potential in layout order, then one CTA per panel sums its
  * entries with no gather (16 bytes per entry, all streamed; for gathered axes
  * too long to stage once per panel); 0 auto (the default) -- staged while
- * P * m_other * 4 <= 6 * nnz * 8, else two-pass.  The setting is process-wide
+ * P * m_other * 4 <= 4 * nnz * 8, else two-pass.  The setting is process-wide
  * and read whenever a layout's geometry is computed (sinkslot_tiles_bytes,
  * sinkslot_tiles_geometry, sinkslot_build_tiles, the solve entry points): a
  * layout must be built and used under the same setting.  A two-pass layout is

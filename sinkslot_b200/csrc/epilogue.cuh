@@ -38,16 +38,17 @@ __device__ __forceinline__ void peer_cta_done(const PeerOut& po, unsigned int* d
 // blend `(1 - alpha) * x + alpha * cand` (:361-363), the marginal proxy
 // `|a * exp(old - new) - a|` (:280-283, :405-412) and the potential change
 // `|new - prev|` (:250-254).
+// The same with the segment's inputs already loaded: b = base[seg] (has_base),
+// old = self_old[seg] (read when OUT == kOutBlend or CHK == kChkMarg), prv =
+// prev[seg] (read when CHK == kChkPot) -- so that a caller can have several
+// segments' loads in flight before it finishes any of them.
 template <int OUT, int CHK>
-__device__ __forceinline__ void segment_epilogue(int64_t seg, float lse, const float* base,
-                                                 const float* self_old, float* out, float w_old,
-                                                 float w_new, float* prev, uint32_t& chk_bits,
-                                                 const PeerOut& po) {
-  const float b = base ? base[seg] : 0.0f;
-  const float res = base ? __fsub_rn(b, lse) : lse;
+__device__ __forceinline__ void segment_epilogue_loaded(int64_t seg, float lse, bool has_base,
+                                                        float b, float old, float prv, float* out,
+                                                        float w_old, float w_new, float* prev,
+                                                        uint32_t& chk_bits, const PeerOut& po) {
+  const float res = has_base ? __fsub_rn(b, lse) : lse;
   float nv = res;
-  float old = 0.0f;
-  if (OUT == kOutBlend || CHK == kChkMarg) old = self_old[seg];
   if (OUT == kOutBlend) nv = __fadd_rn(__fmul_rn(w_old, old), __fmul_rn(w_new, res));
   if (OUT != kOutNone) {
     out[seg] = nv;
@@ -60,9 +61,21 @@ __device__ __forceinline__ void segment_epilogue(int64_t seg, float lse, const f
     const float t = __fmul_rn(ea, expf(__fsub_rn(old, res)));
     chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(t, ea)));
   } else if (CHK == kChkPot) {
-    chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(nv, prev[seg])));
+    chk_bits = max(chk_bits, nonneg_float_bits(__fsub_rn(nv, prv)));
     prev[seg] = nv;
   }
+}
+
+template <int OUT, int CHK>
+__device__ __forceinline__ void segment_epilogue(int64_t seg, float lse, const float* base,
+                                                 const float* self_old, float* out, float w_old,
+                                                 float w_new, float* prev, uint32_t& chk_bits,
+                                                 const PeerOut& po) {
+  const float b = base ? base[seg] : 0.0f;
+  const float old = (OUT == kOutBlend || CHK == kChkMarg) ? self_old[seg] : 0.0f;
+  const float prv = CHK == kChkPot ? prev[seg] : 0.0f;
+  segment_epilogue_loaded<OUT, CHK>(seg, lse, base != nullptr, b, old, prv, out, w_old, w_new,
+                                    prev, chk_bits, po);
 }
 
 template <int CHK>

@@ -176,11 +176,11 @@ static_assert(kSumSmem <= kSmemCap, "panel-sum kernel shared memory");
 // potentials into shared memory per half-step (P * m_o * 4 bytes) while the
 // entries are read once (nnz * 8 bytes).  Above it the two-pass kind (16
 // bytes per entry, all streamed) is cheaper.  Measured on B200 (N = M = 2^k,
-// half-step us staged / two-pass): 2^21 (ratio 2.3) 292 / 508, 2^22 (ratio
-// 4.6) 964 / 1067; at 2^24 (ratio 20) the two-pass kind runs 165 iterations/s
-// against the exact kernel's 108.
+// half-step us, staged / two-pass): 2^21 (ratio 2.3) 292 / ~410, 2^22 (ratio
+// 4.6) 964 / 820 -- staged ~ (98 + 76 ratio) us per GB of entries, two-pass
+// ~381 us per GB: equal near a ratio of 3.7.
 #ifndef SINKSLOT_STAGING_RATIO
-#define SINKSLOT_STAGING_RATIO 6.0
+#define SINKSLOT_STAGING_RATIO 4.0
 #endif
 
 static int g_tiles_kind = kTilesAuto;
@@ -1054,6 +1054,104 @@ __device__ __forceinline__ uint32_t* row_lo(unsigned char* smem, uint32_t roff) 
   return reinterpret_cast<uint32_t*>(smem + kLoOff + roff);
 }
 
+// Row state of a panel (sigma, high and low sums at byte offsets SIG, HI, LO,
+// one flag bit per row), set up and finished by NT threads.  Each thread has
+// the global loads of kRowBatch rows in flight before it uses any of them
+// (rows one at a time would cost one memory round trip each).
+#ifndef SINKSLOT_ROW_BATCH
+#define SINKSLOT_ROW_BATCH 4
+#endif
+constexpr int kRowBatch = SINKSLOT_ROW_BATCH;
+
+__device__ __forceinline__ float radix_to_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// sigma of every panel row (the stabiliser: a.sigma, else base - self_old),
+// zero sums, and the flag bits of rows longer than kMaxTiledRow (handed back
+// from the start); row R (the dummy row of the padding) and any row past the
+// panel's end get sigma 0.  Warp w initialises rows 32 w .. 32 w + 31, then
+// 32 (w + NT/32) ...
+template <int OUT, uint32_t SIG, uint32_t HI, uint32_t LO, int NT>
+__device__ __forceinline__ void panel_rows_init(const TKArgs& a, unsigned char* smem,
+                                                uint32_t* flags, int64_t row0, int rows,
+                                                int warp, int lane) {
+  for (int c0 = warp * 32; c0 <= a.R; c0 += NT * kRowBatch) {
+    float sg[kRowBatch];
+    bool longrow[kRowBatch];
+#pragma unroll
+    for (int k = 0; k < kRowBatch; ++k) {
+      const int r = c0 + k * NT + lane;
+      sg[k] = 0.0f;
+      longrow[k] = false;
+      if (r < rows && OUT != kOutMax) {
+        sg[k] = a.sigma ? a.sigma[row0 + r] : __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
+        longrow[k] = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kRowBatch; ++k) {
+      const int r0 = c0 + k * NT;  // warp-uniform
+      if (r0 > a.R) break;
+      const int r = r0 + lane;
+      if (r <= a.R) {
+        const uint32_t roff = 4u * (uint32_t)r;
+        *reinterpret_cast<float*>(smem + SIG + roff) = sg[k];
+        *reinterpret_cast<uint32_t*>(smem + HI + roff) = 0u;
+        *reinterpret_cast<uint32_t*>(smem + LO + roff) = 0u;
+      }
+      const uint32_t word = __ballot_sync(0xffffffffu, longrow[k]);
+      if (lane == 0) flags[r0 >> 5] = word;
+    }
+  }
+}
+
+// Each panel row's result from its sums: the largest term (max pass), the
+// hand-back to the exact pass (flagged, or a sum below 2^-8), or lse = sigma +
+// log(sum) and the epilogue.  Thread tid takes rows tid, tid + NT, ...
+template <int OUT, int CHK, uint32_t SIG, uint32_t HI, uint32_t LO, int NT>
+__device__ __forceinline__ void panel_rows_finish(const TKArgs& a, unsigned char* smem,
+                                                  const uint32_t* flags, int64_t row0, int rows,
+                                                  int tid, uint32_t& chk_bits) {
+  for (int c0 = tid; c0 < rows; c0 += NT * kRowBatch) {
+    float b[kRowBatch], old[kRowBatch], prv[kRowBatch];
+#pragma unroll
+    for (int k = 0; k < kRowBatch; ++k) {
+      const int r = c0 + k * NT;
+      b[k] = old[k] = prv[k] = 0.0f;
+      if (OUT != kOutMax && r < rows) {
+        const int64_t seg = row0 + r;
+        b[k] = a.base[seg];
+        if (OUT == kOutBlend || CHK == kChkMarg) old[k] = a.self_old[seg];
+        if (CHK == kChkPot) prv[k] = a.prev[seg];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kRowBatch; ++k) {
+      const int r = c0 + k * NT;
+      if (r >= rows) break;
+      const int64_t seg = row0 + r;
+      const uint32_t roff = 4u * (uint32_t)r;
+      const uint32_t hi = *reinterpret_cast<const uint32_t*>(smem + HI + roff);
+      if (OUT == kOutMax) {
+        a.out[seg] = hi ? radix_to_float(hi) : -INFINITY;
+        continue;
+      }
+      const unsigned long long q =
+          ((unsigned long long)hi << kLoBits) + *reinterpret_cast<const uint32_t*>(smem + LO + roff);
+      const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
+      if (flagged || q < kFixMin) {
+        a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
+        continue;
+      }
+      const float tot = (float)((double)q * kFixInv);
+      const float lse = __fadd_rn(*reinterpret_cast<const float*>(smem + SIG + roff), logf(tot));
+      segment_epilogue_loaded<OUT, CHK>(seg, lse, true, b[k], old[k], prv[k], a.out, a.w_old,
+                                        a.w_new, a.prev, chk_bits, a.peers);
+    }
+  }
+}
+
 // One entry {meta, lam bits} against ring stage S: the exponent d = lam +
 // potential[column] - sigma of its term, and its row's byte offset.  Padding
 // entries name the dummy row with lam = -inf, so d = -inf and the term is an
@@ -1167,9 +1265,6 @@ __device__ __forceinline__ void process_group_max(unsigned char* smem, const uin
   }
 }
 
-__device__ __forceinline__ float radix_to_float(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
-}
 
 // A consumer warp's groups of one tile -- slabs [0, nsl) of the entries from
 // e0 -- against ring stage S.  Each group is loaded one ahead (in `en`): behind
@@ -1341,23 +1436,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     const int64_t pb = (int64_t)p * a.B;
     // row state (warp w initialises rows 32w .. 32w+31, then 32(w+31) ...) and
     // flag words: rows longer than kMaxTiledRow are handed back from the start
-    for (int r0 = warp * 32; r0 <= a.R; r0 += kConsumers) {
-      const int r = r0 + lane;
-      bool longrow = false;
-      if (r <= a.R) {
-        const uint32_t roff = 4u * (uint32_t)r;
-        float sg = 0.0f;
-        if (r < rows && OUT != kOutMax) {
-          sg = a.sigma ? a.sigma[row0 + r] : __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
-          longrow = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
-        }
-        *row_sigma(smem, roff) = sg;
-        *row_hi(smem, roff) = 0u;
-        *row_lo(smem, roff) = 0u;
-      }
-      const uint32_t word = __ballot_sync(0xffffffffu, longrow);
-      if (lane == 0) flags[r0 >> 5] = word;
-    }
+    panel_rows_init<OUT, kSigOff, kHiOff, kLoOff, kConsumers>(a, smem, flags, row0, rows, warp,
+                                                              lane);
     // Tile b holds slabs [e0, e1) / 32 of the layout.  Warp w takes groups of
     // kGroup consecutive slabs starting at kGroup*w, kGroup*(w + warps), ...
     // Its groups, taken in order across the panel's tiles, are loaded one
@@ -1395,25 +1475,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
     }
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
     if (*abort_w) break;
-    for (int r = tid; r < rows; r += kConsumers) {
-      const int64_t seg = row0 + r;
-      const uint32_t roff = 4u * (uint32_t)r;
-      const uint32_t hi = *row_hi(smem, roff);
-      if (OUT == kOutMax) {
-        a.out[seg] = hi ? radix_to_float(hi) : -INFINITY;
-        continue;
-      }
-      const unsigned long long q = ((unsigned long long)hi << kLoBits) + *row_lo(smem, roff);
-      const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
-      if (flagged || q < kFixMin) {
-        a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
-        continue;
-      }
-      const float tot = (float)((double)q * kFixInv);
-      const float lse = __fadd_rn(*row_sigma(smem, roff), logf(tot));
-      segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
-                                 chk_bits, a.peers);
-    }
+    panel_rows_finish<OUT, CHK, kSigOff, kHiOff, kLoOff, kConsumers>(a, smem, flags, row0, rows,
+                                                                      tid, chk_bits);
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory");
   }
   chain_release();
@@ -1434,9 +1497,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
 // same layout:
 //   block_gather_kernel: CTA (b, q) copies block b of the gathered potential
 //     into shared memory once and walks the tiles (p, b) of the panels p of
-//     chunk q, one warp per tile; each slot's exponent lam + potential[column]
-//     is stored at the slot's own index of the exponent array (coalesced
-//     8-byte loads, 4-byte stores; padding slots give -inf);
+//     chunk q in work items of at most 32 slabs; each slot's exponent lam +
+//     potential[column] is stored at the slot's own index of the exponent
+//     array (coalesced 2- and 4-byte loads and 4-byte stores; padding slots
+//     give -inf);
 //   panel_sum_kernel: one CTA per panel streams the panel's slots (tiles
 //     (p, 0 .. B-1) are contiguous) -- the row byte offset and the exponent --
 //     and sums exp(exponent - sigma) into the row state exactly as the staged
@@ -1469,13 +1533,32 @@ __device__ __forceinline__ bool layout_matches(const int64_t* header, int kind, 
   return header[1] == kind && header[2] == P && header[3] == B;
 }
 
-// slots [e0, e1) of the split arrays into L2 (tile ranges start on 32-slot
-// boundaries and span whole slabs: 64- and 128-byte multiples)
-__device__ __forceinline__ void prefetch_gather_tile(const uint16_t* coloff, const float* lamv,
-                                                     int64_t e0, int64_t e1) {
-  if (e1 <= e0) return;
-  prefetch_l2(coloff + e0, (uint32_t)(e1 - e0) * 2u);
-  prefetch_l2(lamv + e0, (uint32_t)(e1 - e0) * 4u);
+// The block-gather CTA's tiles (p, b), p in its chunk, cut into work items of at
+// most kItemSlabs slabs (a tile of the 2^24 problem is one item of ~24 slabs,
+// one of 2^20 ~7 items of 32): a table in shared memory after the potential
+// block holds each tile's first slot, its slabs and the items before it
+// (exclusive prefix).  Warp w takes items w, w + kGatherWarps, ...; while it
+// works on one, the slots of its next are prefetched into L2.  (One warp per
+// whole tile left most warps idle where a CTA's chunk has few, large tiles.)
+constexpr int kGatherMaxChunk = 768;  // tiles per CTA (table: 9 KB)
+constexpr int kItemSlabs = 32;
+
+__host__ __device__ __forceinline__ size_t gather_table_off(int logW) {
+  return (size_t)4 << logW;
+}
+// the potential block, then the table: first slots, slab counts and item
+// prefixes of kGatherMaxChunk tiles (+ the total)
+__host__ __device__ __forceinline__ size_t gather_smem(int logW) {
+  return gather_table_off(logW) + (size_t)kGatherMaxChunk * 8 + (size_t)(kGatherMaxChunk + 1) * 4;
+}
+
+// slots of slabs [0, ns) from slot s0 of the split arrays into L2 (tile ranges
+// start on 32-slot boundaries: 64- and 128-byte aligned, whole slabs)
+__device__ __forceinline__ void prefetch_item(const uint16_t* coloff, const float* lamv,
+                                              uint32_t s0, int ns) {
+  if (ns <= 0) return;
+  prefetch_l2(coloff + s0, (uint32_t)ns * kSlab * 2u);
+  prefetch_l2(lamv + s0, (uint32_t)ns * kSlab * 4u);
 }
 
 __global__ void __launch_bounds__(kGatherThreads, kGatherCtasPerSm)
@@ -1489,15 +1572,56 @@ __global__ void __launch_bounds__(kGatherThreads, kGatherCtasPerSm)
   }
   const int b = blockIdx.x;
   const int p0 = blockIdx.y * a.pchunk;
-  const int p1 = min(a.P, p0 + a.pchunk);
-  // the warp's first tile: bounds now, slots into L2 while the previous launch
-  // finishes (the layout is static)
-  int p = p0 + warp;
-  int64_t e0 = 0, e1 = 0;
-  if (p < p1) {
-    e0 = a.tstart[(int64_t)p * a.B + b];
-    e1 = a.tstart[(int64_t)p * a.B + b + 1];
-    if (lane == 0) prefetch_gather_tile(a.coloff, a.lamv, e0, e1);
+  const int nt = max(0, min(a.P, p0 + a.pchunk) - p0);  // <= kGatherMaxChunk
+  uint32_t* te0 = reinterpret_cast<uint32_t*>(potb + gather_table_off(a.logW));
+  int32_t* tsl = reinterpret_cast<int32_t*>(te0 + kGatherMaxChunk);
+  int32_t* ipre = tsl + kGatherMaxChunk;
+  // the tile table (the layout is static: built while the previous launch
+  // finishes); slots < 2^32 because nnz < 2^32
+  for (int i = tid; i < nt; i += kGatherThreads) {
+    const int64_t t = (int64_t)(p0 + i) * a.B + b;
+    const int64_t s0 = a.tstart[t];
+    const int ns = (int)((a.tstart[t + 1] - s0) >> 5);
+    te0[i] = (uint32_t)s0;
+    tsl[i] = ns;
+    ipre[i] = (ns + kItemSlabs - 1) / kItemSlabs;  // items of tile i, for now
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // exclusive prefix of the item counts, in place: each lane sums its own run
+    // [i0, i1), a warp scan gives the runs' offsets, each lane rewrites its run
+    const int per = (nt + 31) / 32;
+    const int i0 = min(nt, lane * per), i1 = min(nt, i0 + per);
+    int run = 0;
+    for (int i = i0; i < i1; ++i) run += ipre[i];
+    int incl = run;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int acc = incl - run;
+    for (int i = i0; i < i1; ++i) {
+      const int c = ipre[i];
+      ipre[i] = acc;
+      acc += c;
+    }
+    if (lane == 31) ipre[nt] = incl;
+  }
+  __syncthreads();
+  const int items = ipre[nt];
+  int cur = 0;  // the tile of the warp's latest located item (items only grow)
+  // item j: its first slot and slabs
+  auto locate = [&](int j, uint32_t& s0, int& ns) {
+    while (ipre[cur + 1] <= j) ++cur;
+    const int sub = j - ipre[cur];
+    s0 = te0[cur] + (uint32_t)(sub * kItemSlabs * kSlab);
+    ns = min(kItemSlabs, tsl[cur] - sub * kItemSlabs);
+  };
+  uint32_t s0 = 0;
+  int ns = 0;
+  if (warp < items) {
+    locate(warp, s0, ns);
+    if (lane == 0) prefetch_item(a.coloff, a.lamv, s0, ns);
   }
   chain_enter();
   if (*(volatile int*)a.err != 0) return;  // an earlier launch failed: do nothing
@@ -1506,40 +1630,38 @@ __global__ void __launch_bounds__(kGatherThreads, kGatherCtasPerSm)
   float* pot = reinterpret_cast<float*>(potb);
   for (int i = tid; i < cnt; i += kGatherThreads) pot[i] = a.other[c0 + i];
   __syncthreads();
-  for (; p < p1; p += kGatherWarps) {
-    // the warp's next tile: bounds loaded and slots prefetched a tile ahead
-    const int pn = p + kGatherWarps;
-    int64_t f0 = 0, f1 = 0;
-    if (pn < p1) {
-      f0 = a.tstart[(int64_t)pn * a.B + b];
-      f1 = a.tstart[(int64_t)pn * a.B + b + 1];
-      if (lane == 0) prefetch_gather_tile(a.coloff, a.lamv, f0, f1);
+  for (int j = warp; j < items; j += kGatherWarps) {
+    // the warp's next item: located and prefetched while this one is processed
+    uint32_t n0 = 0;
+    int nns = 0;
+    if (j + kGatherWarps < items) {
+      locate(j + kGatherWarps, n0, nns);
+      if (lane == 0) prefetch_item(a.coloff, a.lamv, n0, nns);
     }
-    const int nsl = (int)((e1 - e0) >> 5);
-    const uint16_t* cs = a.coloff + e0 + lane;
-    const float* ls = a.lamv + e0 + lane;
-    float* dst = a.expo + e0 + lane;
+    const uint16_t* cs = a.coloff + s0 + lane;
+    const float* ls = a.lamv + s0 + lane;
+    float* dst = a.expo + s0 + lane;
     int s = 0;
-    for (; s + kGatherUnroll <= nsl; s += kGatherUnroll) {
+    for (; s + kGatherUnroll <= ns; s += kGatherUnroll) {
       uint32_t c[kGatherUnroll];
       float l[kGatherUnroll];
 #pragma unroll
-      for (int j = 0; j < kGatherUnroll; ++j) {
-        c[j] = ld_stream(cs + (s + j) * kSlab);
-        l[j] = ld_stream(ls + (s + j) * kSlab);
+      for (int u = 0; u < kGatherUnroll; ++u) {
+        c[u] = ld_stream(cs + (s + u) * kSlab);
+        l[u] = ld_stream(ls + (s + u) * kSlab);
       }
 #pragma unroll
-      for (int j = 0; j < kGatherUnroll; ++j)
-        __stcs(dst + (s + j) * kSlab,
-               __fadd_rn(l[j], *reinterpret_cast<const float*>(potb + c[j])));
+      for (int u = 0; u < kGatherUnroll; ++u)
+        __stcs(dst + (s + u) * kSlab,
+               __fadd_rn(l[u], *reinterpret_cast<const float*>(potb + c[u])));
     }
-    for (; s < nsl; ++s) {
+    for (; s < ns; ++s) {
       const uint32_t c = ld_stream(cs + s * kSlab);
       __stcs(dst + s * kSlab,
              __fadd_rn(ld_stream(ls + s * kSlab), *reinterpret_cast<const float*>(potb + c)));
     }
-    e0 = f0;
-    e1 = f1;
+    s0 = n0;
+    ns = nns;
   }
   chain_release();
 }
@@ -1614,23 +1736,8 @@ __global__ void __launch_bounds__(kSumThreads, 1) panel_sum_kernel(const TKArgs 
     if (rows <= 0) break;
     // row state and flag words (rows longer than kMaxTiledRow are handed back
     // from the start)
-    for (int r0 = warp * 32; r0 <= a.R; r0 += kSumThreads) {
-      const int r = r0 + lane;
-      bool longrow = false;
-      if (r <= a.R) {
-        const uint32_t roff = 4u * (uint32_t)r;
-        float sg = 0.0f;
-        if (r < rows && OUT != kOutMax) {
-          sg = a.sigma ? a.sigma[row0 + r] : __fsub_rn(a.base[row0 + r], a.self_old[row0 + r]);
-          longrow = a.ptr[row0 + r + 1] - a.ptr[row0 + r] > kMaxTiledRow;
-        }
-        *row_sigma2(smem, roff) = sg;
-        *row_hi2(smem, roff) = 0u;
-        *row_lo2(smem, roff) = 0u;
-      }
-      const uint32_t word = __ballot_sync(0xffffffffu, longrow);
-      if (lane == 0) flags[r0 >> 5] = word;
-    }
+    panel_rows_init<OUT, kSigOff2, kHiOff2, kLoOff2, kSumThreads>(a, smem, flags, row0, rows,
+                                                                  warp, lane);
     const int64_t e0 = a.tstart[(int64_t)p * a.B];
     const int nsl = (int)((a.tstart[(int64_t)(p + 1) * a.B] - e0) >> 5);
     if (!entered) {
@@ -1702,25 +1809,8 @@ __global__ void __launch_bounds__(kSumThreads, 1) panel_sum_kernel(const TKArgs 
       }
     }
     __syncthreads();
-    for (int r = tid; r < rows; r += kSumThreads) {
-      const int64_t seg = row0 + r;
-      const uint32_t roff = 4u * (uint32_t)r;
-      const uint32_t hi = *row_hi2(smem, roff);
-      if (OUT == kOutMax) {
-        a.out[seg] = hi ? radix_to_float(hi) : -INFINITY;
-        continue;
-      }
-      const unsigned long long q = ((unsigned long long)hi << kLoBits) + *row_lo2(smem, roff);
-      const bool flagged = (flags[r >> 5] >> (r & 31)) & 1u;
-      if (flagged || q < kFixMin) {
-        a.fb_list[atomicAdd(a.fb_count, 1)] = (int)seg;
-        continue;
-      }
-      const float tot = (float)((double)q * kFixInv);
-      const float lse = __fadd_rn(*row_sigma2(smem, roff), logf(tot));
-      segment_epilogue<OUT, CHK>(seg, lse, a.base, a.self_old, a.out, a.w_old, a.w_new, a.prev,
-                                 chk_bits, a.peers);
-    }
+    panel_rows_finish<OUT, CHK, kSigOff2, kHiOff2, kLoOff2, kSumThreads>(a, smem, flags, row0,
+                                                                         rows, tid, chk_bits);
     __syncthreads();
   }
   if (!entered) chain_enter();
@@ -1747,20 +1837,23 @@ static int launch_block_gather(const TiledHalfStep& h, cudaStream_t st) {
   a.other = h.other;
   a.expo = L.expo;
   a.err = h.err;
-  // panel chunks: about four waves of CTAs in all (each restages its block)
+  // panel chunks: about four waves of CTAs in all (each restages its block),
+  // at most kGatherMaxChunk tiles each
   const int64_t waves = 4 * (int64_t)kGatherCtasPerSm * num_sms();
   int64_t Q = std::min<int64_t>(g.P, std::max<int64_t>(1, ceil_div64(waves, g.B)));
+  Q = std::max<int64_t>(Q, ceil_div64(g.P, kGatherMaxChunk));
   a.pchunk = (int)ceil_div64(g.P, Q);
   Q = ceil_div64(g.P, a.pchunk);
-  SINKSLOT_REQUIRE(Q <= 65535, "two-pass half step: too many panel chunks");
-  const size_t smem = (size_t)4 << g.logW;
+  SINKSLOT_REQUIRE(Q <= 65535 && a.pchunk <= kGatherMaxChunk,
+                   "two-pass half step: too many panel chunks");
+  const size_t smem = gather_smem(g.logW);
   static bool configured[64] = {};
   int dev = 0;
   SINKSLOT_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     SINKSLOT_CUDA_TRY(cudaFuncSetAttribute(block_gather_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)(4u << kMaxLogW)));
+                                           (int)gather_smem(kMaxLogW)));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   SINKSLOT_CUDA_TRY(launch_chained(block_gather_kernel, dim3((unsigned)g.B, (unsigned)Q),

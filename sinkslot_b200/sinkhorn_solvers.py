@@ -101,7 +101,7 @@ TILE_MIN_NNZ = 1 << 22
 # half-step); "two_pass" first writes every entry's exponent lam + potential
 # with one CTA per block, then sums each panel's entries without a gather (16
 # bytes per entry, all streamed).  "auto" (the default) takes the staged kind
-# while its staging costs at most 6x the entry stream, else the two-pass kind:
+# while its staging costs at most 4x the entry stream, else the two-pass kind:
 # large gathered axes (N = 2^24 on one GPU, row slices of a many-GPU partition)
 # no longer fall back to the exact kernel's random gathers (about 36 bytes of
 # HBM time per entry).

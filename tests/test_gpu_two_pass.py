@@ -170,7 +170,7 @@ def test_two_pass_equals_staged_stop_modes(cuda, kinds, mode, tol, variant):
 
 def test_two_pass_chosen_for_a_long_gathered_axis(cuda, kinds):
     """Auto policy: 2^16 rows gathering from 2^21 columns (L = 8) stage 148 x 8 MB
-    per half-step, more than 6x the row side's entry stream -- the row side runs
+    per half-step, more than 4x the row side's entry stream -- the row side runs
     two passes, the column side (gathering 2^16) the staged kind; the solve
     agrees with the exact kernel to the tiled-vs-exact bar and with the staged
     kind bit for bit."""
