@@ -1516,6 +1516,11 @@ constexpr int kGatherUnroll = 4;     // slabs a lane has in flight
 constexpr int kSumWarps = 32;
 constexpr int kSumThreads = 32 * kSumWarps;
 constexpr int kSumGroup = 8;         // slabs a warp loads together, one group ahead
+#ifndef SINKSLOT_SUM_PREFETCH
+#define SINKSLOT_SUM_PREFETCH 1
+#endif
+// the group after the one in flight prefetched into L2 by the warp's lane 0
+constexpr bool kSumPrefetch = SINKSLOT_SUM_PREFETCH;
 
 struct BGArgs {
   int64_t m_o;
@@ -1751,7 +1756,8 @@ __global__ void __launch_bounds__(kSumThreads, 1) panel_sum_kernel(const TKArgs 
     __syncthreads();
     uint32_t ron[kSumGroup];
     float xn[kSumGroup];
-    if (lane == 0) prefetch_sum_group(a.rowoff, a.expo, e0, nsl, kSumGroup * warp + kStep);
+    if (kSumPrefetch && lane == 0)
+      prefetch_sum_group(a.rowoff, a.expo, e0, nsl, kSumGroup * warp + kStep);
     load_sum_group(a.rowoff, a.expo, e0, nsl, kSumGroup * warp, lane, ron, xn);
     for (int g = kSumGroup * warp; g < nsl; g += kStep) {
       uint32_t ro[kSumGroup];
@@ -1761,7 +1767,7 @@ __global__ void __launch_bounds__(kSumThreads, 1) panel_sum_kernel(const TKArgs 
         ro[j] = ron[j];
         x[j] = xn[j];
       }
-      if (lane == 0) prefetch_sum_group(a.rowoff, a.expo, e0, nsl, g + 2 * kStep);
+      if (kSumPrefetch && lane == 0) prefetch_sum_group(a.rowoff, a.expo, e0, nsl, g + 2 * kStep);
       load_sum_group(a.rowoff, a.expo, e0, nsl, g + kStep, lane, ron, xn);
       const int cnt = nsl - g;
       if (OUT == kOutMax) {
