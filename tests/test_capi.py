@@ -79,3 +79,53 @@ def test_null_arguments_rejected_without_touching_a_device(lib):
     st = lib.sinkslot_build_support(None, None, None, None, 10, 10, 3, None, None, None, 4, 0,
                                     None, 0, ctypes.byref(nnz), None)
     assert st == 1 and b"null" in lib.sinkslot_last_error()
+
+
+def _align256(x):
+    return (x + 255) // 256 * 256
+
+
+def test_tiles_kind_policy_and_geometry(lib):
+    """The tiled kind per side: staged while staging the gathered potential
+    (P panels x m_other x 4 bytes) costs at most 4x the entry stream (nnz x 8
+    bytes), else two-pass; the setting is process-wide and validated; a
+    two-pass layout is the staged one plus four per-slot arrays, its panels up
+    to 16383 rows (host logic only, no device work; 148 SMs assumed here)."""
+    kind = ctypes.c_int(-1)
+    geom = (ctypes.c_int * 5)()
+    assert lib.sinkslot_get_tiles_kind(ctypes.byref(kind)) == 0 and kind.value == 0
+    try:
+        for log2n, want in [(20, 1), (21, 1), (22, 2), (24, 2)]:
+            n = 1 << log2n
+            nnz = 64 * n
+            assert lib.sinkslot_tiles_geometry(n, n, nnz, geom) == 0
+            P = geom[0]
+            assert lib.sinkslot_tiles_kind_of(n, n, nnz, ctypes.byref(kind)) == 0
+            assert kind.value == want, (log2n, kind.value)
+            # the rule itself, on the staged geometry
+            assert lib.sinkslot_set_tiles_kind(1) == 0
+            assert lib.sinkslot_tiles_geometry(n, n, nnz, geom) == 0
+            staged_P = geom[0]
+            assert (staged_P * n * 4 <= 4 * nnz * 8) == (want == 1)
+            assert lib.sinkslot_set_tiles_kind(0) == 0
+            del P
+        # a forced kind, its geometry and the layout bytes
+        n, m, nnz = 1 << 20, 1 << 20, 64 << 20
+        sizes = {}
+        for k in (1, 2):
+            assert lib.sinkslot_set_tiles_kind(k) == 0
+            lb, bb = ctypes.c_int64(0), ctypes.c_int64(0)
+            assert lib.sinkslot_tiles_bytes(n, m, nnz, ctypes.byref(lb), ctypes.byref(bb)) == 0
+            assert lib.sinkslot_tiles_geometry(n, m, nnz, geom) == 0
+            P, R, B, logW, smem = list(geom)
+            assert P * R >= n and R + 1 <= (16384 if k == 2 else 8320) and smem <= 227 * 1024
+            cap = nnz + 63 * P * B
+            staged = _align256(64) + _align256(8 * (P * B + 1)) + _align256(8 * cap)
+            extra = 2 * _align256(2 * cap) + 2 * _align256(4 * cap) if k == 2 else 0
+            assert lb.value == staged + extra
+            sizes[k] = (P, R, B, logW)
+        # the two-pass kind keeps the blocks and takes longer panels
+        assert sizes[2][2:] == sizes[1][2:] and sizes[2][1] >= sizes[1][1]
+        assert lib.sinkslot_set_tiles_kind(3) == 1 and b"kind" in lib.sinkslot_last_error()
+    finally:
+        lib.sinkslot_set_tiles_kind(0)
