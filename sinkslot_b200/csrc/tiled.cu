@@ -1512,7 +1512,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) tiled_half_step_kernel(const 
 constexpr int kGatherWarps = 16;
 constexpr int kGatherThreads = 32 * kGatherWarps;
 constexpr int kGatherCtasPerSm = 3;  // 64 KB blocks: three per SM
-constexpr int kGatherUnroll = 4;     // slabs a lane has in flight
+#ifndef SINKSLOT_GATHER_UNROLL
+#define SINKSLOT_GATHER_UNROLL 8
+#endif
+constexpr int kGatherUnroll = SINKSLOT_GATHER_UNROLL;  // slabs a lane has in flight
 constexpr int kSumWarps = 32;
 constexpr int kSumThreads = 32 * kSumWarps;
 constexpr int kSumGroup = 8;         // slabs a warp loads together, one group ahead
