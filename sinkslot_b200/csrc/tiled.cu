@@ -847,6 +847,9 @@ static int build_tiles_body(const int32_t* ptr, const void* idx, int idx_bytes,
   SINKSLOT_REQUIRE(g.P > 0 && g.B > 0, "build_tiles: empty geometry");
   SINKSLOT_REQUIRE((int64_t)g.P * g.B < (int64_t(1) << (32 - kBankBits)),
                    "build_tiles: too many tiles");
+  // the two-pass exponent pass addresses slots with 32-bit indices
+  SINKSLOT_REQUIRE(g.kind != kTilesTwoPass || g.cap < (int64_t(1) << 32),
+                   "build_tiles: a two-pass layout must hold fewer than 2^32 slots");
   LayoutPtrs L = carve_layout(layout, g);
   if (g.direct) {
     if (idx_bytes == 2)
